@@ -1,0 +1,526 @@
+"""Benchmark of the B200 GQA flash-attention forward (driver contract).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload prefill|decode|chunked|long_decode]
+
+Default workload (BASELINE metric "prefill TFLOP/s @8K causal; decode HBM GB/s
+& us @16K KV"): Llama-3.1-8B-shape causal prefill B=1 per GPU, Hq=32, Hkv=8,
+D=128, S=8192, bf16, inputs N(0,1) from a CUDA generator seeded by rank
+(configs[1] of BASELINE.json); the same line carries the 16K-KV split-KV decode
+(configs[2]) under "decode_16k". With N GPUs (torchrun) every rank runs its own
+batch element (batch sharding, no communication: weak scaling).
+
+A step is one gqa_flash_attn call. Each step is timed by CUDA events on the
+launching stream; L2 (126 MB) is flushed between steps by writing a 256 MB
+buffer (outside the events). `value` is algorithmic FLOPs (causal pairs only)
+or algorithmic bytes of all ranks / max-over-ranks time. `e2e` repeats the
+metric through the public API with pinned host inputs copied in and the output
+copied back inside the timed region.
+
+--impl reference times the reference's CPU path (the numpy port of
+tests/reference.py in oracle/) on the host cores on a bounded sample of the
+same workload; under torchrun only rank 0 runs it.
+"""
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "gqa-flash-attn-rtx3060_b200"))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "prefill TFLOP/s @8K causal; decode HBM GB/s & µs @16K KV (1/2/4/8 B200)"
+FLUSH_BYTES = 256 << 20
+
+
+# ----------------------------------------------------------------------------- workloads
+def causal_pairs(sq, skv, causal=True):
+    """Number of (query, key) pairs a causal (bottom-right) attention evaluates."""
+    if not causal:
+        return sq * skv
+    off = skv - sq
+    i = np.arange(sq, dtype=np.int64)
+    return int(np.clip(i + off + 1, 0, skv).sum())
+
+
+def attn_flops(B, Hq, Sq, Skv, D, causal=True):
+    return 4.0 * B * Hq * D * causal_pairs(Sq, Skv, causal)
+
+
+def attn_bytes(B, Hq, Hkv, Sq, Skv, D, elem=2):
+    """Compulsory HBM bytes: K + V read once, Q read once, O written once."""
+    return float(elem * (2 * B * Hkv * Skv * D + 2 * B * Hq * Sq * D))
+
+
+WORKLOADS = {
+    # name: (B per rank, Hq, Hkv, Sq, Skv, D, bound, scaling)
+    "prefill": dict(B=1, Hq=32, Hkv=8, Sq=8192, Skv=8192, D=128, bound="tensor", scaling="weak",
+                    name="llama3.1-8b-prefill-8k (config 2)"),
+    "decode": dict(B=1, Hq=32, Hkv=8, Sq=1, Skv=16384, D=128, bound="hbm", scaling="weak",
+                   name="split-kv-decode-16k (config 3)"),
+    "chunked": dict(B=4, Hq=32, Hkv=8, Sq=512, Skv=16384, D=128, bound="tensor", scaling="strong",
+                    name="chunked-prefill-b4-512x16k (config 4), batch x kv-head sharded"),
+    "long_decode": dict(B=64, Hq=64, Hkv=8, Sq=1, Skv=131072, D=128, bound="hbm", scaling="strong",
+                        name="long-decode-b64-131k (config 5), seq_kv sharded + NCCL LSE combine"),
+}
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return dict(hbm=p["hbm_gbs"], bf16=p["bf16_tflops"], bf16_sus=p.get("bf16_tflops_sustained"),
+                    source="measured")
+    return dict(hbm=6650.0, bf16=1590.0, bf16_sus=1400.0, source="fallback")
+
+
+def profile_traffic(kernel_key):
+    """Per-launch DRAM bytes of a kernel from a committed ncu summary (profiles/*.txt), or None."""
+    pdir = os.path.join(ROOT, "profiles")
+    if not os.path.isdir(pdir):
+        return None
+    for fn in sorted(os.listdir(pdir)):
+        if not fn.endswith(".txt"):
+            continue
+        with open(os.path.join(pdir, fn)) as f:
+            for line in f:
+                if line.startswith(f"traffic_bytes_per_launch[{kernel_key}]:"):
+                    try:
+                        return float(line.split(":", 1)[1].split()[0])
+                    except ValueError:
+                        return None
+    return None
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, device):
+        self.proc = None
+        self.out = tempfile.NamedTemporaryFile(prefix="clocks_", suffix=".csv", delete=False)
+        try:
+            pr = torch.cuda.get_device_properties(device)
+            self.target = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+        except Exception:
+            self.target = str(device)
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.target, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.out, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.out.close()
+        rows = []
+        with open(self.out.name) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) != 10:
+                    continue
+                try:
+                    rows.append(dict(sm=float(parts[1]), smax=float(parts[2]), util=float(parts[4]),
+                                     reasons={n: parts[6 + i] for i, n in enumerate(self.REASONS)}))
+                except ValueError:
+                    continue
+        os.unlink(self.out.name)
+        if not rows:
+            return None
+        load = [r for r in rows if r["util"] >= 50] or rows
+        reasons = sorted({n for r in load for n, v in r["reasons"].items() if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r["sm"] for r in load), "sm_max_mhz": max(r["smax"] for r in rows),
+                "reasons": reasons, "samples": len(rows), "samples_under_load": len(load)}
+
+
+# ----------------------------------------------------------------------------- distributed plumbing
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    elif n_gpus > 1:
+        raise SystemExit("--gpus N > 1 needs torchrun (one process per GPU)")
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world, device):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------- timing
+def timed_steps(step_fn, steps, warmup, world, device, flush=None, stream=None):
+    """Runs warmup + steps; each timed step bracketed by CUDA events on `stream`.
+    Returns (per-step ms list, wall ms of the whole timed loop)."""
+    stream = stream or torch.cuda.current_stream(device)
+    for _ in range(warmup):
+        step_fn(0)
+        if flush is not None:
+            flush()
+    pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    barrier(world)
+    torch.cuda.synchronize(device)
+    t0 = time.perf_counter()
+    for i in range(steps):
+        if flush is not None:
+            flush()
+        torch.cuda._sleep(100000)  # ~50 us: gives the host a head start so the events bracket only the step
+        pairs[i][0].record(stream)
+        step_fn(i)
+        pairs[i][1].record(stream)
+    torch.cuda.synchronize(device)
+    wall = (time.perf_counter() - t0) * 1e3
+    barrier(world)
+    return [a.elapsed_time(b) for a, b in pairs], wall
+
+
+def make_flush(device):
+    buf = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
+
+    def flush():
+        buf.fill_(1)
+    return flush
+
+
+# ----------------------------------------------------------------------------- our arm
+def run_attention_workload(wl, world, rank, device, steps, warmup, args):
+    from gqa_kernels import gqa_flash_attn
+    from gqa_kernels import sharded as S
+    B, Hq, Hkv, Sq, Skv, D = wl["B"], wl["Hq"], wl["Hkv"], wl["Sq"], wl["Skv"], wl["D"]
+    dt = torch.bfloat16
+    gen = torch.Generator(device=device).manual_seed(rank)
+    flops_total = attn_flops(B, Hq, Sq, Skv, D) * (world if wl["scaling"] == "weak" else 1)
+    bytes_total = attn_bytes(B, Hq, Hkv, Sq, Skv, D) * (world if wl["scaling"] == "weak" else 1)
+
+    def rnd(*shape):
+        return torch.randn(*shape, generator=gen, device=device, dtype=torch.float32).to(dt)
+
+    name = args.workload
+    local = {}
+    if name in ("prefill", "decode"):
+        local["q"], local["k"], local["v"] = rnd(B, Hq, Sq, D), rnd(B, Hkv, Skv, D), rnd(B, Hkv, Skv, D)
+        # decode: K+V (67 MB) fit in L2, so three input copies rotate (201 MB) instead of a flush
+        copies = 3 if name == "decode" else 1
+        sets = [(local["q"], local["k"], local["v"])]
+        for _ in range(copies - 1):
+            sets.append(tuple(t.clone() for t in sets[0]))
+
+        def step(i):
+            q, k, v = sets[i % len(sets)]
+            local["o"] = gqa_flash_attn(q, k, v, causal=True)
+        flush = make_flush(device) if copies == 1 else None
+        launches_per_step = 1
+    elif name == "chunked":
+        br, hr = S.shard_units(B, Hkv, world, rank)
+        g = Hq // Hkv
+        nb, nh = br[1] - br[0], hr[1] - hr[0]
+        q, k, v = rnd(nb, nh * g, Sq, D), rnd(nb, nh, Skv, D), rnd(nb, nh, Skv, D)
+
+        def step(i):
+            local["o"] = S.head_sharded_forward(q, k, v)
+        flush = make_flush(device)
+        launches_per_step = 1
+    elif name == "long_decode":
+        k0, k1 = S.kv_range(Skv, world, rank)
+        q = torch.randn(B, Hq, Sq, D, generator=torch.Generator(device=device).manual_seed(0), device=device).to(dt)
+        k, v = rnd(B, Hkv, k1 - k0, D), rnd(B, Hkv, k1 - k0, D)
+        if world == 1:
+            def step(i):
+                local["o"] = gqa_flash_attn(q, k, v, causal=True)
+            launches_per_step = 1
+        else:
+            packed = torch.empty(S.packed_size(q.shape), dtype=torch.float32, device=device)
+            gathered = torch.empty((world, packed.numel()), dtype=torch.float32, device=device)
+
+            def step(i):
+                S.partial_forward(q, k, v, True, k0, Skv, out=packed)
+                S.gather_partials(packed, out=gathered)
+                local["o"] = S.combine_partials(gathered, tuple(q.shape), dt, device)
+            launches_per_step = 2
+        flush = None
+    else:
+        raise SystemExit(f"unknown workload {name}")
+
+    clock = ClockSampler(device) if rank == 0 else None
+    if clock:
+        clock.start()
+    times, wall = timed_steps(step, steps, warmup, world, device, flush=flush)
+    clocks = clock.stop() if clock else None
+    mean_ms = statistics.mean(times)
+    total_ms = max_over_ranks(sum(times), world, device)
+    ms_step = total_ms / steps
+    res = dict(ms_per_step=ms_step, mean_ms_rank0=mean_ms, median_ms_rank0=statistics.median(times),
+               wall_ms=wall, clocks=clocks, launches=steps * launches_per_step,
+               flops=flops_total, bytes=bytes_total, local=local)
+    if wl["bound"] == "tensor":
+        res["value"] = flops_total / (ms_step * 1e-3) / 1e12
+        res["unit"] = "TFLOP/s"
+    else:
+        res["value"] = bytes_total / (ms_step * 1e-3) / 1e9
+        res["unit"] = "GB/s"
+    return res
+
+
+def run_e2e(wl, world, rank, device, steps, args):
+    """Same metric through the public API with pinned host buffers: H2D of q/k/v,
+    gqa_flash_attn, D2H of o, all inside the timed region."""
+    from gqa_kernels import gqa_flash_attn
+    B, Hq, Hkv, Sq, Skv, D = wl["B"], wl["Hq"], wl["Hkv"], wl["Sq"], wl["Skv"], wl["D"]
+    if args.workload not in ("prefill", "decode"):
+        return None
+    g = torch.Generator().manual_seed(rank)
+    qh = torch.randn(B, Hq, Sq, D, generator=g).to(torch.bfloat16).pin_memory()
+    kh = torch.randn(B, Hkv, Skv, D, generator=g).to(torch.bfloat16).pin_memory()
+    vh = torch.randn(B, Hkv, Skv, D, generator=g).to(torch.bfloat16).pin_memory()
+    oh = torch.empty(B, Hq, Sq, D, dtype=torch.bfloat16).pin_memory()
+    qd, kd, vd = (torch.empty(t.shape, dtype=t.dtype, device=device) for t in (qh, kh, vh))
+
+    def step(i):
+        qd.copy_(qh, non_blocking=True)
+        kd.copy_(kh, non_blocking=True)
+        vd.copy_(vh, non_blocking=True)
+        o = gqa_flash_attn(qd, kd, vd, causal=True)
+        oh.copy_(o, non_blocking=True)
+    times, _ = timed_steps(step, steps, 2, world, device)
+    ms = max_over_ranks(sum(times), world, device) / steps
+    mult = world if wl["scaling"] == "weak" else 1
+    h2d = sum(t.numel() * t.element_size() for t in (qh, kh, vh))
+    d2h = oh.numel() * oh.element_size()
+    if wl["bound"] == "tensor":
+        val, unit = attn_flops(B, Hq, Sq, Skv, D) * mult / (ms * 1e-3) / 1e12, "TFLOP/s"
+    else:
+        val, unit = attn_bytes(B, Hq, Hkv, Sq, Skv, D) * mult / (ms * 1e-3) / 1e9, "GB/s"
+    return {"value": round(val, 3), "unit": unit, "ms_per_step": round(ms, 4),
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+
+
+# ----------------------------------------------------------------------------- CPU baseline (oracle)
+def cpu_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+        return max(n) if n else 1
+    except Exception:
+        return 1
+
+
+def cpu_sample(wl, budget_s, steps=None):
+    """Times the oracle port of tests/reference.py on blocks of query rows of the
+    workload (one kv head's query heads at a time). Returns (value, unit, sample text, per-step s)."""
+    from oracle import gqa_oracle as O
+    B, Hq, Hkv, Sq, Skv, D = wl["B"], wl["Hq"], wl["Hkv"], wl["Sq"], wl["Skv"], wl["D"]
+    G = Hq // Hkv
+    rng = np.random.default_rng(0)
+    rows = Sq if Sq <= 64 else 256  # query rows per sample step
+    q = rng.standard_normal((1, G, Sq, D), dtype=np.float32)
+    k = rng.standard_normal((1, 1, Skv, D), dtype=np.float32)
+    v = rng.standard_normal((1, 1, Skv, D), dtype=np.float32)
+    q, k, v = (O.bf16_round(x) for x in (q, k, v))
+    done_flops = done_bytes = 0.0
+    elapsed = 0.0
+    n = 0
+    per = []
+    off = Skv - Sq
+    while (steps is None and (elapsed < budget_s or n == 0)) or (steps is not None and n < steps):
+        r0 = (n * rows * 37) % max(1, Sq - rows + 1) if Sq > rows else 0
+        r1 = min(Sq, r0 + rows)
+        # rows r0..r1 of one (b, kv head): keys up to the last row's causal bound
+        kend = min(Skv, r1 + off)
+        t0 = time.perf_counter()
+        O.gqa_reference(q[:, :, r0:r1], k[:, :, :kend], v[:, :, :kend], causal=True)
+        dt = time.perf_counter() - t0
+        per.append(dt)
+        elapsed += dt
+        pairs = int(np.clip(np.arange(r0, r1) + off + 1, 0, Skv).sum())
+        done_flops += 4.0 * G * D * pairs
+        done_bytes += 2.0 * (2 * kend * D + 2 * G * (r1 - r0) * D)
+        n += 1
+    if wl["bound"] == "tensor":
+        val, unit = done_flops / elapsed / 1e12, "TFLOP/s"
+    else:
+        val, unit = done_bytes / elapsed / 1e9, "GB/s"
+    sample = (f"{n} step(s) of {rows} query rows x {G} query heads of one (batch, kv head) unit of the "
+              f"workload, fp32 numpy oracle; {elapsed:.2f} s")
+    return val, unit, sample, per
+
+
+# ----------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="prefill")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the decode half of the default line")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    wl = WORKLOADS[args.workload]
+    default_steps = {"prefill": 1000, "decode": 5000, "chunked": 500, "long_decode": 100}[args.workload]
+    steps = args.steps or default_steps
+
+    if args.impl == "reference":
+        return main_reference(args, wl, steps)
+
+    world, rank, local = dist_setup(args.gpus)
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    import gqa_kernels._lib as L
+    L.load()
+    peaks = measured_peaks()
+
+    res = run_attention_workload(wl, world, rank, device, steps, args.warmup, args)
+    line = {
+        "metric": METRIC if args.workload in ("prefill", "decode") else f"{args.workload} {res['unit']}",
+        "value": round(res["value"], 3),
+        "unit": res["unit"],
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(res["ms_per_step"], 5),
+        "higher_is_better": True,
+        "scaling": wl["scaling"],
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (N(0,1) bf16, CUDA generator seeded by rank)",
+        "config": {"workload": wl["name"], "batch_per_gpu" if wl["scaling"] == "weak" else "batch": wl["B"],
+                   "num_heads": wl["Hq"], "num_kv_heads": wl["Hkv"], "seq_q": wl["Sq"], "seq_kv": wl["Skv"],
+                   "head_dim": wl["D"], "causal": True,
+                   "l2": "flushed between steps (256 MB write)" if args.workload in ("prefill", "chunked")
+                   else "inputs larger than L2 (rotating copies)" if args.workload == "decode"
+                   else "inputs larger than L2 (32 GiB K/V)",
+                   "parallelism": (f"batch-sharded x{world}" if wl["scaling"] == "weak" else
+                                   f"kv-head/batch x{world}" if args.workload == "chunked" else
+                                   f"seq_kv x{world} + NCCL all-gather LSE combine")},
+        "gpu_launches": res["launches"],
+    }
+    # roofline of the dominant kernel, from rank 0's mean per-launch event time. Per-rank
+    # work: one workload instance (weak scaling) or 1/world of it (strong scaling).
+    launch_ms = res["mean_ms_rank0"]
+    share = 1.0 if wl["scaling"] == "weak" else 1.0 / world
+    if wl["bound"] == "tensor":
+        work = attn_flops(wl["B"], wl["Hq"], wl["Sq"], wl["Skv"], wl["D"]) * share
+        achieved = work / (launch_ms * 1e-3) / 1e12
+        line["roofline"] = {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16"],
+                            "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16"], 4),
+                            "frac_of_sustained": (round(achieved / peaks["bf16_sus"], 4)
+                                                  if peaks["bf16_sus"] else None),
+                            "peak_source": f"{peaks['source']} bf16 dense burst (MEASURED_PEAKS.json)",
+                            "work_per_launch": work, "traffic": profile_traffic(args.workload)}
+    else:
+        work = attn_bytes(wl["B"], wl["Hq"], wl["Hkv"], wl["Sq"], wl["Skv"], wl["D"]) * share
+        achieved = work / (launch_ms * 1e-3) / 1e9
+        line["roofline"] = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm"], "unit": "GB/s",
+                            "frac": round(achieved / peaks["hbm"], 4),
+                            "peak_source": f"{peaks['source']} HBM copy (MEASURED_PEAKS.json)",
+                            "work_per_launch": work, "traffic": profile_traffic(args.workload)}
+    line["clocks"] = res["clocks"]
+
+    # decode half of the headline metric
+    if args.workload == "prefill" and not args.no_decode:
+        dwl = WORKLOADS["decode"]
+        dargs = argparse.Namespace(**{**vars(args), "workload": "decode"})
+        dres = run_attention_workload(dwl, world, rank, device, 5000, args.warmup, dargs)
+        dl_ms = dres["mean_ms_rank0"]
+        dbytes = attn_bytes(1, 32, 8, 1, 16384, 128)
+        line["decode_16k"] = {"value": round(dres["value"], 1), "unit": "GB/s",
+                              "us_per_step": round(dres["ms_per_step"] * 1e3, 2),
+                              "steps": 5000, "scaling": "weak",
+                              "roofline": {"bound": "hbm", "achieved": round(dbytes / (dl_ms * 1e-3) / 1e9, 1),
+                                           "peak": peaks["hbm"], "unit": "GB/s",
+                                           "frac": round(dbytes / (dl_ms * 1e-3) / 1e9 / peaks["hbm"], 4),
+                                           "traffic": profile_traffic("decode")},
+                              "clocks": dres["clocks"]}
+        line["gpu_launches"] += dres["launches"]
+
+    if not args.no_e2e:
+        e2e = run_e2e(wl, world, rank, device, 20 if args.workload == "prefill" else 200, args)
+        if e2e is not None:
+            line["e2e"] = e2e
+
+    if rank == 0 and world == 1 and not args.no_cpu:
+        val, unit, sample, _ = cpu_sample(wl, budget_s=12.0)
+        line["cpu_baseline"] = {"value": round(val, 5), "unit": unit, "cores": cpu_threads(), "kind": "port",
+                                "sample": sample}
+
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def main_reference(args, wl, steps):
+    """The reference arm: the reference's CPU path (numpy port of tests/reference.py)."""
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    # each step is one block of query rows; run as many of the requested warmup + steps
+    # as fit in about two minutes (at least 3)
+    _, _, _, per = cpu_sample(wl, budget_s=0.0, steps=1)
+    total = steps + args.warmup
+    n_run = max(3, min(total, int(120.0 / max(per[0], 1e-3))))
+    val, unit, sample, per = cpu_sample(wl, budget_s=0.0, steps=n_run)
+    ms_step = statistics.mean(per) * 1e3
+    line = {
+        "metric": METRIC if args.workload in ("prefill", "decode") else f"{args.workload} {unit}",
+        "value": round(val, 6), "unit": unit, "impl": "reference", "n_gpus": world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 3), "higher_is_better": True,
+        "scaling": wl["scaling"], "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": wl["name"], "num_heads": wl["Hq"], "num_kv_heads": wl["Hkv"], "seq_q": wl["Sq"],
+                   "seq_kv": wl["Skv"], "head_dim": wl["D"], "causal": True},
+        "cpu_baseline": {"value": round(val, 6), "unit": unit, "cores": cpu_threads(), "kind": "port",
+                         "sample": sample + f"; {n_run} of {total} requested steps run (bounded)"},
+        "e2e": {"value": round(val, 6), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

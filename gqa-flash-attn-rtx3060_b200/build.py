@@ -1,0 +1,70 @@
+"""Builds libgqa_sm100.so (the C-ABI library) in-tree for sm_100a.
+
+    python gqa-flash-attn-rtx3060_b200/build.py [--force]
+
+The library is one translation unit (csrc/gqa_sm100.cu) compiled by nvcc with
+`-gencode arch=compute_100a,code=sm_100a` and the static CUDA runtime; it does
+not link libcuda (the driver's tensor-map encoder is looked up at run time),
+so it loads on a machine without a GPU driver.
+"""
+import argparse
+import os
+import shutil
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join(HERE, "csrc")
+INCLUDE = os.path.join(os.path.dirname(HERE), "include")
+OUT = os.path.join(HERE, "gqa_kernels", "libgqa_sm100.so")
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-lineinfo", "-std=c++17",
+    "-Xcompiler", "-fPIC", "-shared",
+    "-cudart", "static",
+]
+
+
+def _sources():
+    return sorted(
+        [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cu", ".cuh"))]
+        + [os.path.join(INCLUDE, f) for f in os.listdir(INCLUDE) if f.endswith(".h")]
+    )
+
+
+def up_to_date():
+    if not os.path.exists(OUT):
+        return False
+    t = os.path.getmtime(OUT)
+    return all(os.path.getmtime(s) <= t for s in _sources())
+
+
+def nvcc():
+    path = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not os.path.exists(path):
+        raise RuntimeError("nvcc not found; the CUDA toolkit is required to build libgqa_sm100.so")
+    return path
+
+
+def build(force=False, verbose=False):
+    """Compiles the library unless it is newer than every source. Returns its path."""
+    if not force and up_to_date():
+        return OUT
+    tmp = OUT + ".tmp"
+    cmd = [nvcc(), *NVCC_FLAGS, "-I", INCLUDE, "-o", tmp, os.path.join(CSRC, "gqa_sm100.cu")]
+    if verbose:
+        cmd.insert(1, "-Xptxas=-v")
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    os.replace(tmp, OUT)
+    return OUT
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("-v", "--verbose", action="store_true")
+    a = ap.parse_args()
+    print(build(force=a.force, verbose=a.verbose))
+    sys.exit(0)

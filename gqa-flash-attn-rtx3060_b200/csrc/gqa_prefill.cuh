@@ -1,0 +1,388 @@
+// tcgen05 / TMEM / TMA GQA forward for many packed query rows (prefill and
+// chunked prefill).
+//
+// One CTA owns two 128-row query tiles of one (batch, kv_head). A tile packs
+// the group's `group` query heads x `bm = 128 / group` consecutive positions
+// into the 128 rows of one UMMA (row r -> head kv*group + r / bm, position
+// p + r % bm), the group packing of gqa_kernels/gqa_fwd.py:57-65, done here by
+// one 4-D TMA box {64, bm, group, 1}. K and V tiles of 128 keys stream through
+// a ring of shared-memory slots filled by a TMA producer warp.
+//
+// Per key tile j and query tile i (i = 0, 1):
+//   MMA warp (one thread):  S_i = Q_i K_j^T          (SS UMMA, f32 into TMEM)
+//   softmax warpgroup i:    P_i = exp2(S_i*scale - m) (bf16/f16 written back into TMEM over S_i)
+//   MMA warp:               O_i += P_i V_j            (TS UMMA: A = P from TMEM, B = V from smem)
+// The two tiles ping-pong so one warpgroup's exp2 work overlaps the other
+// tile's MMAs. The running max is only moved when it grows by more than
+// 2^8 (values of P stay <= 256), so O in TMEM is rescaled rarely.
+//
+// Causal semantics (gqa_kernels/gqa_fwd.py:70-73, :94-96): the key loop of a
+// CTA ends at the last key any of its rows can see; row r masks keys beyond
+// its own position + (seq_kv - seq_q). Only the last one or two key tiles of a
+// CTA need the mask.
+#pragma once
+
+#include "gqa_common.cuh"
+
+namespace gqa {
+
+struct PrefillParams {
+  int batch, hq, hkv, group, seq_q, seq_kv;
+  int bm;       // positions per tile = 128 / group
+  int n_pairs;  // ceil(ceil(seq_q / bm) / 2)
+  int causal;
+  float scale_log2;
+};
+
+template <int HD>
+struct PrefillCfg {
+  static constexpr int kRows = 128;                  // packed rows per query tile (UMMA M)
+  static constexpr int kBN = 128;                    // keys per tile (UMMA N of S, K of PV)
+  static constexpr int kNSub = HD / 64;              // 128-byte swizzle sub-tiles along d
+  static constexpr int kSubBytes = 128 * 128;        // 128 rows x 128 B
+  static constexpr int kTileBytes = kNSub * kSubBytes;  // one Q, K or V tile
+  static constexpr int kSlots = (HD == 128) ? 4 : 8;    // K/V ring slots (K and V alternate)
+  static constexpr int kQOff = 0;
+  static constexpr int kKVOff = 2 * kTileBytes;
+  static constexpr int kBarOff = kKVOff + kSlots * kTileBytes;
+  // barriers: q_full[2] kv_full[S] kv_empty[S] s_full[2] p_full[2] o_final[2] mma_done
+  static constexpr int kNumBars = 2 + 2 * kSlots + 2 + 2 + 2 + 1;
+  static constexpr int kMiscOff = kBarOff + kNumBars * 8;  // tmem base, abort flag
+  static constexpr int kSmemBytes = kMiscOff + 16 + 1024;  // + alignment slack
+  // warps 0-3 softmax tile 0, 4-7 softmax tile 1, 8 MMA issuer, 9 TMA producer, 10-11 idle
+  static constexpr int kThreads = 384;
+  static constexpr int kTmemCols = 512;
+  // setmaxnreg split. The launch holds kThreads x (registers per thread at launch)
+  // registers; the split needs 2 x 128 x kSoftmaxRegs + 128 x kControlRegs of them.
+  // gqa_sm100.cu checks the compiled register count before every launch.
+  static constexpr int kSoftmaxRegs = 208;
+  static constexpr int kControlRegs = 88;
+  static constexpr int kRegsNeeded = 256 * kSoftmaxRegs + 128 * kControlRegs;  // 64512 = 384 x 168
+  static constexpr int kColS0 = 0, kColS1 = 128, kColO0 = 256, kColO1 = 256 + HD;
+};
+
+template <int HD, bool BF16>
+__global__ void __launch_bounds__(384, 1)
+    gqa_prefill_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap qmap,
+                       const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                       const __grid_constant__ CUtensorMap omap) {
+  using Cfg = PrefillCfg<HD>;
+  constexpr int NSUB = Cfg::kNSub;
+  constexpr int SLOTS = Cfg::kSlots;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_base = smem_u32(smem_raw);
+  const uint32_t base = (raw_base + 1023u) & ~1023u;
+  uint8_t* const smem = smem_raw + (base - raw_base);
+
+  const uint32_t q_smem0 = base + Cfg::kQOff;
+  const uint32_t kv_smem0 = base + Cfg::kKVOff;
+  const uint32_t bars = base + Cfg::kBarOff;
+  const uint32_t bar_q_full = bars;                      // [2]
+  const uint32_t bar_kv_full = bars + 16;                // [SLOTS]
+  const uint32_t bar_kv_empty = bar_kv_full + 8 * SLOTS; // [SLOTS]
+  const uint32_t bar_s_full = bar_kv_empty + 8 * SLOTS;  // [2]
+  const uint32_t bar_p_full = bar_s_full + 16;           // [2]
+  const uint32_t bar_o_final = bar_p_full + 16;          // [2]
+  const uint32_t bar_mma_done = bar_o_final + 16;
+  uint32_t* tmem_base_ptr = reinterpret_cast<uint32_t*>(smem + Cfg::kMiscOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kMiscOff + 4);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+
+  // ---- work item: longest (highest) query pair first, across all (b, kv) ----
+  const int bh_count = p.batch * p.hkv;
+  const int bh = blockIdx.x % bh_count;
+  const int pair = p.n_pairs - 1 - blockIdx.x / bh_count;
+  const int b = bh / p.hkv;
+  const int kvh = bh % p.hkv;
+  const int p0 = pair * 2 * p.bm;  // first position of tile 0
+  const int off = p.seq_kv - p.seq_q;
+  int kv_end = p.seq_kv;
+  if (p.causal) kv_end = min(kv_end, min(p0 + 2 * p.bm, p.seq_q) + off);
+  const int nk = (kv_end > 0) ? (kv_end + Cfg::kBN - 1) / Cfg::kBN : 0;
+
+  if (tid == 0) {
+    mbar_init(bar_q_full, 1);
+    mbar_init(bar_q_full + 8, 1);
+    for (int s = 0; s < SLOTS; ++s) {
+      mbar_init(bar_kv_full + 8 * s, 1);
+      mbar_init(bar_kv_empty + 8 * s, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar_s_full + 8 * i, 1);
+      mbar_init(bar_p_full + 8 * i, 128);
+      mbar_init(bar_o_final + 8 * i, 1);
+    }
+    mbar_init(bar_mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 8) {
+    tmem_alloc(smem_u32(tmem_base_ptr), Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_ptr;
+
+  // Register split: 2 x 208 (softmax warpgroups) + 88 (control warpgroup) = 504 per thread-slot,
+  // i.e. 64512 registers = the 384 x 168 the kernel is launched with.
+  static_assert(Cfg::kSoftmaxRegs == 208 && Cfg::kControlRegs == 88, "keep the asm immediates in sync");
+  if (warp >= 8) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 88;" ::: "memory");
+  if (warp == 9) {
+    // ================================================================ producer
+    if (lane == 0 && nk > 0) {
+      tma_prefetch_desc(&qmap);
+      tma_prefetch_desc(&kmap);
+      tma_prefetch_desc(&vmap);
+      const int hq0 = kvh * p.group;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        mbar_arrive_expect_tx(bar_q_full + 8 * i, Cfg::kTileBytes);
+#pragma unroll
+        for (int s = 0; s < NSUB; ++s)
+          tma_load_4d(q_smem0 + i * Cfg::kTileBytes + s * Cfg::kSubBytes, &qmap, bar_q_full + 8 * i, s * 64,
+                      p0 + i * p.bm, hq0, b);
+      }
+      int t = 0;
+      const int n_loads = 2 * nk;
+      for (; t < n_loads; ++t) {
+        const int slot = t % SLOTS;
+        const int use = t / SLOTS;
+        if (use > 0 && !mbar_wait(bar_kv_empty + 8 * slot, (use - 1) & 1, abort_flag, 1)) break;
+        const uint32_t full = bar_kv_full + 8 * slot;
+        mbar_arrive_expect_tx(full, Cfg::kTileBytes);
+        const CUtensorMap* map = (t & 1) ? &vmap : &kmap;
+        const int key0 = (t >> 1) * Cfg::kBN;
+#pragma unroll
+        for (int s = 0; s < NSUB; ++s)
+          tma_load_4d(kv_smem0 + slot * Cfg::kTileBytes + s * Cfg::kSubBytes, map, full, s * 64, key0, kvh, b);
+      }
+      if (t < n_loads) {  // aborted: let in-flight loads land before teardown
+        volatile int dummy = 0;
+        for (int u = max(0, t - SLOTS); u < t; ++u)
+          mbar_wait(bar_kv_full + 8 * (u % SLOTS), (u / SLOTS) & 1, &dummy, 2);
+      }
+    }
+  } else if (warp == 8) {
+    // ================================================================ MMA issuer
+    if (lane == 0 && nk > 0) {
+      constexpr uint32_t idesc_qk = make_idesc_f16(128, Cfg::kBN, BF16, false);
+      constexpr uint32_t idesc_pv = make_idesc_f16(128, HD, BF16, true);
+      auto issue_qk = [&](int i, int slot) {
+        const uint32_t tS = tmem_base + (i ? Cfg::kColS1 : Cfg::kColS0);
+        const uint32_t qa = q_smem0 + i * Cfg::kTileBytes;
+        const uint32_t kb = kv_smem0 + slot * Cfg::kTileBytes;
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k) {
+          const uint32_t o = (k >> 2) * Cfg::kSubBytes + (k & 3) * 32;
+          umma_ss(tS, desc_sw128_kmajor(qa + o), desc_sw128_kmajor(kb + o), idesc_qk, k > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_pv = [&](int i, int slot, bool acc) {
+        const uint32_t tS = tmem_base + (i ? Cfg::kColS1 : Cfg::kColS0);
+        const uint32_t tO = tmem_base + (i ? Cfg::kColO1 : Cfg::kColO0);
+        const uint32_t vb = kv_smem0 + slot * Cfg::kTileBytes;
+#pragma unroll
+        for (int k = 0; k < Cfg::kBN / 16; ++k) {
+          // P: 16 keys = 8 TMEM columns of packed 16-bit pairs; V: 16 key rows of 128 B.
+          umma_ts(tO, tS + k * 8, desc_sw128_mnmajor(vb + k * 16 * 128, Cfg::kSubBytes), idesc_pv,
+                  (acc || k > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(bar_q_full, 0, abort_flag, 10) && mbar_wait(bar_q_full + 8, 0, abort_flag, 11) &&
+                mbar_wait(bar_kv_full, 0, abort_flag, 12);
+      if (ok) {
+        tc_fence_after();
+        issue_qk(0, 0);
+        umma_commit(bar_s_full);
+        issue_qk(1, 0);
+        umma_commit(bar_s_full + 8);
+        umma_commit(bar_kv_empty);  // K_0 consumed
+        for (int j = 0; j < nk; ++j) {
+          const int tv = 2 * j + 1, sv = tv % SLOTS;
+          const int tk = 2 * j + 2, sk = tk % SLOTS;
+          if (!mbar_wait(bar_kv_full + 8 * sv, (tv / SLOTS) & 1, abort_flag, 13)) break;
+          if (!mbar_wait(bar_p_full, j & 1, abort_flag, 14)) break;
+          tc_fence_after();
+          issue_pv(0, sv, j > 0);
+          const bool more = (j + 1 < nk);
+          if (more) {
+            if (!mbar_wait(bar_kv_full + 8 * sk, (tk / SLOTS) & 1, abort_flag, 15)) break;
+            tc_fence_after();
+            issue_qk(0, sk);
+            umma_commit(bar_s_full);
+          } else {
+            umma_commit(bar_o_final);
+          }
+          if (!mbar_wait(bar_p_full + 8, j & 1, abort_flag, 16)) break;
+          tc_fence_after();
+          issue_pv(1, sv, j > 0);
+          umma_commit(bar_kv_empty + 8 * sv);  // V_j consumed
+          if (more) {
+            issue_qk(1, sk);
+            umma_commit(bar_s_full + 8);
+            umma_commit(bar_kv_empty + 8 * sk);  // K_{j+1} consumed
+          } else {
+            umma_commit(bar_o_final + 8);
+          }
+        }
+      }
+      // Drain: every MMA issued above completes before TMEM is released.
+      umma_commit(bar_mma_done);
+      volatile int dummy = 0;
+      mbar_wait(bar_mma_done, 0, &dummy, 17);
+    }
+    __syncwarp();
+  }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 208;" ::: "memory");
+    // ================================================================ softmax warpgroups
+    const int wg = warp >> 2;    // query tile handled by this warpgroup
+    const int row = tid & 127;   // packed row == TMEM lane
+    const int wq = warp & 3;     // TMEM lane quarter of this warp
+    const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
+    const uint32_t tS = tmem_base + lane_off + (wg ? Cfg::kColS1 : Cfg::kColS0);
+    const uint32_t tO = tmem_base + lane_off + (wg ? Cfg::kColO1 : Cfg::kColO0);
+    const uint32_t s_full = bar_s_full + 8 * wg;
+    const uint32_t p_full = bar_p_full + 8 * wg;
+
+    const int g = row / p.bm;
+    const int pos = p0 + wg * p.bm + (row - g * p.bm);
+    int lim = p.seq_kv;  // number of keys this row may see
+    if (p.causal) lim = min(lim, pos + off + 1);
+    const float scale = p.scale_log2;
+
+    float m_run = -INFINITY;
+    float l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nk; ++j) {
+      ok = mbar_wait(s_full, j & 1, abort_flag, 20 + wg);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t sr[128];
+      tmem_ld32(tS + 0, sr + 0);
+      tmem_ld32(tS + 32, sr + 32);
+      tmem_ld32(tS + 64, sr + 64);
+      tmem_ld32(tS + 96, sr + 96);
+      tmem_wait_ld();
+      reg_fence(sr);
+      const int rem = lim - j * Cfg::kBN;  // visible columns in this tile
+      if (rem < Cfg::kBN) {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) sr[c] = (c < rem) ? sr[c] : __float_as_uint(-INFINITY);
+      }
+      float mx0 = __uint_as_float(sr[0]), mx1 = __uint_as_float(sr[1]);
+      float mx2 = __uint_as_float(sr[2]), mx3 = __uint_as_float(sr[3]);
+#pragma unroll
+      for (int c = 4; c < 128; c += 4) {
+        mx0 = fmaxf(mx0, __uint_as_float(sr[c]));
+        mx1 = fmaxf(mx1, __uint_as_float(sr[c + 1]));
+        mx2 = fmaxf(mx2, __uint_as_float(sr[c + 2]));
+        mx3 = fmaxf(mx3, __uint_as_float(sr[c + 3]));
+      }
+      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * scale;
+      const float m_new = fmaxf(m_run, mx);
+      const bool need = m_new > m_run + 8.0f;  // false while both are -inf
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        const float alpha = need ? fast_exp2(m_run - m_new) : 1.0f;
+#pragma unroll
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t orr[32];
+          tmem_ld32(tO + c * 32, orr);
+          tmem_wait_ld();
+          reg_fence(orr);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) orr[e] = __float_as_uint(__uint_as_float(orr[e]) * alpha);
+          tmem_st32(tO + c * 32, orr);
+        }
+        tmem_wait_st();
+      }
+      if (need) {
+        l_run *= fast_exp2(m_run - m_new);
+        m_run = m_new;
+      }
+      const float nm = -m_run;
+      float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float a = fast_exp2(fmaf(__uint_as_float(sr[32 * c + 2 * e]), scale, nm));
+          const float bb = fast_exp2(fmaf(__uint_as_float(sr[32 * c + 2 * e + 1]), scale, nm));
+          sum0 += a;
+          sum1 += bb;
+          pk[e] = pack2<BF16>(a, bb);
+        }
+        tmem_st16(tS + c * 16, pk);
+      }
+      l_run += sum0 + sum1;
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+
+    // ---- epilogue: O / l -> 16-bit -> swizzled staging (this tile's Q buffer) -> TMA store
+    bool have_o = ok && nk > 0;
+    if (have_o) {
+      have_o = mbar_wait(bar_o_final + 8 * wg, 0, abort_flag, 22 + wg);
+      have_o = __all_sync(0xffffffffu, have_o);
+    }
+    if (have_o) tc_fence_after();
+    const float inv = 1.0f / l_run;  // l == 0 -> inf -> NaN rows, as the reference's 0/0
+    const uint32_t stage = q_smem0 + wg * Cfg::kTileBytes;
+#pragma unroll
+    for (int c = 0; c < HD / 32; ++c) {
+      uint32_t orr[32];
+      if (have_o) {
+        tmem_ld32(tO + c * 32, orr);
+        tmem_wait_ld();
+        reg_fence(orr);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) orr[e] = __float_as_uint(__int_as_float(0x7fc00000));
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int chunk = 4 * c + e;  // 16-byte chunk along d (8 values)
+#define GQA_OV(i) (__uint_as_float(orr[8 * e + (i)]) * inv)
+        const uint32_t w0 = pack2<BF16>(GQA_OV(0), GQA_OV(1));
+        const uint32_t w1 = pack2<BF16>(GQA_OV(2), GQA_OV(3));
+        const uint32_t w2 = pack2<BF16>(GQA_OV(4), GQA_OV(5));
+        const uint32_t w3 = pack2<BF16>(GQA_OV(6), GQA_OV(7));
+#undef GQA_OV
+        const uint32_t dst = stage + (chunk >> 3) * Cfg::kSubBytes + sw128_off(row, chunk & 7);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(w0), "r"(w1), "r"(w2), "r"(w3)
+                     : "memory");
+      }
+    }
+    fence_proxy_async_smem();
+    if (wg == 0)
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+    else
+      asm volatile("bar.sync 2, 128;" ::: "memory");
+    const int tile_pos = p0 + wg * p.bm;
+    if (row == 0 && tile_pos < p.seq_q) {
+#pragma unroll
+      for (int s = 0; s < NSUB; ++s)
+        tma_store_4d(&omap, stage + s * Cfg::kSubBytes, s * 64, tile_pos, kvh * p.group, b);
+      bulk_commit_group();
+      bulk_wait_group0();
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 8) tmem_dealloc(tmem_base, Cfg::kTmemCols);
+}
+
+}  // namespace gqa

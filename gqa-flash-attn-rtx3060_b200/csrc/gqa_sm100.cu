@@ -1,0 +1,569 @@
+// libgqa_sm100.so: host side of the C ABI declared in include/gqa_sm100.h.
+//
+// Validates arguments (returning GQA_ERR_* before any launch), builds the TMA
+// tensor maps, sizes the launch for the current device's SM count and
+// enqueues the kernels on the caller's stream. Nothing here allocates device
+// memory or synchronises (except gqa_device_error, which says so).
+#include <mutex>
+#include <vector>
+
+#include "gqa_common.cuh"
+#include "gqa_combine.cuh"
+#include "gqa_prefill.cuh"
+#include "gqa_stream.cuh"
+
+namespace gqa {
+namespace {
+
+// ----------------------------------------------------------------------------- device cache
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+struct DeviceState {
+  bool ready = false;
+  int status = GQA_OK;
+  int sm_count = 0;
+};
+
+// The prefill kernel rebalances registers with setmaxnreg; the increase can only
+// be granted if the launch reserved enough registers (threads x registers per
+// thread). Refuse to launch a build where that does not hold: the request would
+// never be granted and the kernel would not finish.
+template <typename K>
+int check_reg_split(K kernel, int threads, int needed) {
+  cudaFuncAttributes a;
+  if (cudaFuncGetAttributes(&a, kernel) != cudaSuccess) return GQA_ERR_CUDA;
+  return (a.numRegs * threads >= needed) ? GQA_OK : GQA_ERR_UNSUPPORTED;
+}
+
+std::mutex g_mutex;
+std::vector<DeviceState> g_devices;
+EncodeTiledFn g_encode = nullptr;
+
+template <typename K>
+cudaError_t set_smem(K kernel, int bytes) {
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+int init_device(int dev) {
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return GQA_ERR_CUDA;
+  if (prop.major != 10) return GQA_ERR_NO_DEVICE;
+  if (!g_encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || fn == nullptr)
+      return GQA_ERR_CUDA;
+    g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+  }
+  cudaError_t e = cudaSuccess;
+  auto chk = [&](cudaError_t x) { if (x != cudaSuccess && e == cudaSuccess) e = x; };
+  chk(set_smem(gqa_prefill_kernel<128, true>, PrefillCfg<128>::kSmemBytes));
+  chk(set_smem(gqa_prefill_kernel<128, false>, PrefillCfg<128>::kSmemBytes));
+  chk(set_smem(gqa_prefill_kernel<64, true>, PrefillCfg<64>::kSmemBytes));
+  chk(set_smem(gqa_prefill_kernel<64, false>, PrefillCfg<64>::kSmemBytes));
+  if (e != cudaSuccess) return GQA_ERR_CUDA;
+  int rs = check_reg_split(gqa_prefill_kernel<128, true>, PrefillCfg<128>::kThreads, PrefillCfg<128>::kRegsNeeded);
+  if (!rs) rs = check_reg_split(gqa_prefill_kernel<128, false>, PrefillCfg<128>::kThreads, PrefillCfg<128>::kRegsNeeded);
+  if (!rs) rs = check_reg_split(gqa_prefill_kernel<64, true>, PrefillCfg<64>::kThreads, PrefillCfg<64>::kRegsNeeded);
+  if (!rs) rs = check_reg_split(gqa_prefill_kernel<64, false>, PrefillCfg<64>::kThreads, PrefillCfg<64>::kRegsNeeded);
+  if (rs) return rs;
+#define GQA_SET_STREAM(HD, BF, RG) chk(set_smem(gqa_stream_kernel<HD, BF, RG>, StreamCfg<HD>::kSmemBytes))
+  GQA_SET_STREAM(128, true, 1); GQA_SET_STREAM(128, true, 2); GQA_SET_STREAM(128, true, 4);
+  GQA_SET_STREAM(128, false, 1); GQA_SET_STREAM(128, false, 2); GQA_SET_STREAM(128, false, 4);
+  GQA_SET_STREAM(64, true, 1); GQA_SET_STREAM(64, true, 2); GQA_SET_STREAM(64, true, 4);
+  GQA_SET_STREAM(64, false, 1); GQA_SET_STREAM(64, false, 2); GQA_SET_STREAM(64, false, 4);
+#undef GQA_SET_STREAM
+  if (e != cudaSuccess) return GQA_ERR_CUDA;
+  return GQA_OK;
+}
+
+// Returns GQA_OK and the SM count of the current device, initialising it once.
+int current_device(int* sm_count) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return GQA_ERR_NO_DEVICE;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if ((int)g_devices.size() <= dev) g_devices.resize(dev + 1);
+  DeviceState& st = g_devices[dev];
+  if (!st.ready) {
+    st.status = init_device(dev);
+    if (st.status == GQA_OK) {
+      if (cudaDeviceGetAttribute(&st.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        st.status = GQA_ERR_CUDA;
+    }
+    st.ready = true;
+  }
+  if (sm_count) *sm_count = st.sm_count;
+  return st.status;
+}
+
+// ----------------------------------------------------------------------------- validation
+struct Shape {
+  int batch, hq, hkv, group, seq_q, seq_kv, head_dim;
+};
+
+int check_shape(int batch, int hq, int hkv, int seq_q, int seq_kv, int head_dim, Shape* s) {
+  if (batch < 0 || hq <= 0 || hkv <= 0 || seq_q < 0 || seq_kv < 0) return GQA_ERR_INVALID_ARG;
+  if (hq % hkv != 0) return GQA_ERR_INVALID_ARG;
+  if (head_dim != 64 && head_dim != 128) return GQA_ERR_UNSUPPORTED;
+  const int g = hq / hkv;
+  if (g > 128 || (g & (g - 1)) != 0) return GQA_ERR_UNSUPPORTED;  // packed tiles need a power-of-two group
+  *s = Shape{batch, hq, hkv, g, seq_q, seq_kv, head_dim};
+  return GQA_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// (b, h, s, d) strides of a 16-bit tensor: d stride 1, the others multiples of 8 elements.
+int check_strides(const void* ptr, const int64_t* st) {
+  if (!ptr || !st) return GQA_ERR_INVALID_ARG;
+  if (!aligned16(ptr)) return GQA_ERR_ALIGNMENT;
+  if (st[3] != 1) return GQA_ERR_ALIGNMENT;
+  for (int i = 0; i < 3; ++i)
+    if (st[i] < 0 || (st[i] % 8) != 0) return GQA_ERR_ALIGNMENT;
+  return GQA_OK;
+}
+
+// 4-D tensor map over a (b, h, s, d) 16-bit tensor, box {64, box_s, box_h, 1}, 128-byte swizzle.
+int make_map(CUtensorMap* map, const void* ptr, const int64_t* st, int b, int h, int s, int d, int box_s,
+             int box_h) {
+  cuuint64_t dims[4] = {(cuuint64_t)d, (cuuint64_t)s, (cuuint64_t)h, (cuuint64_t)b};
+  cuuint64_t strides[3] = {(cuuint64_t)st[2] * 2, (cuuint64_t)st[1] * 2, (cuuint64_t)st[0] * 2};
+  // Degenerate strides (size-1 dims) may be 0 in caller metadata; TMA wants a valid stride.
+  if (s == 1 && strides[0] == 0) strides[0] = (cuuint64_t)d * 2;
+  if (h == 1 && strides[1] == 0) strides[1] = strides[0] * s;
+  if (b == 1 && strides[2] == 0) strides[2] = strides[1] * h;
+  for (int i = 0; i < 3; ++i)
+    if (strides[i] == 0 || (strides[i] & 15) != 0 || strides[i] >= (1ull << 40)) return GQA_ERR_ALIGNMENT;
+  cuuint32_t box[4] = {64u, (cuuint32_t)box_s, (cuuint32_t)box_h, 1u};
+  cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, const_cast<void*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? GQA_OK : GQA_ERR_CUDA;
+}
+
+int launch_status() {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? GQA_OK : GQA_ERR_CUDA;
+}
+
+// ----------------------------------------------------------------------------- streaming plan
+// Number of packed rows (group * block_m) the streaming kernel handles per unit.
+constexpr int kStreamMaxRows = 64;
+constexpr int kStreamCtasPerSm = 2;
+constexpr int kMaxSplits = 64;
+
+struct StreamPlan {
+  int block_m, rows, rg, n_mtiles, units, nsplit, chunk;
+};
+
+StreamPlan plan_stream(const Shape& s, int sm_count, bool allow_split) {
+  StreamPlan pl{};
+  pl.block_m = std::max(1, std::min(s.seq_q, kStreamMaxRows / s.group));
+  pl.rows = s.group * pl.block_m;
+  pl.rg = pl.rows <= 16 ? 1 : (pl.rows <= 32 ? 2 : 4);
+  pl.n_mtiles = (s.seq_q + pl.block_m - 1) / pl.block_m;
+  pl.units = s.batch * s.hkv * pl.n_mtiles;
+  const int stages = std::max(1, (s.seq_kv + 63) / 64);
+  pl.nsplit = 1;
+  pl.chunk = stages * 64;
+  if (!allow_split) return pl;
+  const double slots = (double)sm_count * kStreamCtasPerSm;
+  double best = -1.0;
+  const int max_ns = std::min(std::min(stages, kMaxSplits), std::max(1, 4096 / pl.rows));
+  for (int ns = 1; ns <= max_ns; ++ns) {
+    const int chunk_st = (stages + ns - 1) / ns;
+    const int ns_eff = (stages + chunk_st - 1) / chunk_st;
+    if (ns_eff != ns) continue;
+    const double ctas = (double)pl.units * ns_eff;
+    const double waves = std::ceil(ctas / slots);
+    // fraction of SM-time doing useful streaming, all CTAs of a wave costing chunk_st stages
+    const double eff = ((double)pl.units * stages) / (waves * slots * chunk_st);
+    if (eff > best + 1e-3) {
+      best = eff;
+      pl.nsplit = ns;
+      pl.chunk = chunk_st * 64;
+    }
+  }
+  return pl;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+size_t stream_ws_bytes(const StreamPlan& pl, int head_dim) {
+  const size_t n = (size_t)pl.units * pl.nsplit * pl.rows;
+  return align256(n * 4) * 2 + align256(n * head_dim * 4) + align256((size_t)pl.units * 4);
+}
+
+void stream_ws_carve(const StreamPlan& pl, int head_dim, void* ws, StreamParams* p) {
+  const size_t n = (size_t)pl.units * pl.nsplit * pl.rows;
+  uint8_t* c = reinterpret_cast<uint8_t*>(ws);
+  p->ws_m = reinterpret_cast<float*>(c);
+  c += align256(n * 4);
+  p->ws_l = reinterpret_cast<float*>(c);
+  c += align256(n * 4);
+  p->ws_acc = reinterpret_cast<float*>(c);
+  c += align256(n * head_dim * 4);
+  p->ws_cnt = reinterpret_cast<unsigned*>(c);
+}
+
+bool use_stream(const Shape& s) { return s.group <= kStreamMaxRows && s.group * s.seq_q <= kStreamMaxRows; }
+
+template <int HD, bool BF>
+cudaError_t launch_stream_hd(const StreamParams& p, const StreamPlan& pl, const CUtensorMap& km,
+                             const CUtensorMap& vm, cudaStream_t st) {
+  const dim3 grid(pl.units * pl.nsplit);
+  const int smem = StreamCfg<HD>::kSmemBytes;
+  switch (pl.rg) {
+    case 1: gqa_stream_kernel<HD, BF, 1><<<grid, 160, smem, st>>>(p, km, vm); break;
+    case 2: gqa_stream_kernel<HD, BF, 2><<<grid, 160, smem, st>>>(p, km, vm); break;
+    default: gqa_stream_kernel<HD, BF, 4><<<grid, 160, smem, st>>>(p, km, vm); break;
+  }
+  return cudaGetLastError();
+}
+
+// Fills the common fields of StreamParams and launches.
+int run_stream(const Shape& s, const StreamPlan& pl, StreamParams p, const void* k, const void* v,
+               const int64_t* ks, const int64_t* vs, int dtype, cudaStream_t st) {
+  CUtensorMap km, vm;
+  int rc = make_map(&km, k, ks, s.batch, s.hkv, s.seq_kv, s.head_dim, 64, 1);
+  if (rc) return rc;
+  rc = make_map(&vm, v, vs, s.batch, s.hkv, s.seq_kv, s.head_dim, 64, 1);
+  if (rc) return rc;
+  p.batch = s.batch;
+  p.hq = s.hq;
+  p.hkv = s.hkv;
+  p.group = s.group;
+  p.seq_q = s.seq_q;
+  p.seq_kv = s.seq_kv;
+  p.block_m = pl.block_m;
+  p.n_mtiles = pl.n_mtiles;
+  p.rows = pl.rows;
+  p.nsplit = pl.nsplit;
+  p.chunk = pl.chunk;
+  cudaError_t e;
+  const bool bf = dtype == GQA_DTYPE_BF16;
+  if (s.head_dim == 128)
+    e = bf ? launch_stream_hd<128, true>(p, pl, km, vm, st) : launch_stream_hd<128, false>(p, pl, km, vm, st);
+  else
+    e = bf ? launch_stream_hd<64, true>(p, pl, km, vm, st) : launch_stream_hd<64, false>(p, pl, km, vm, st);
+  return e == cudaSuccess ? GQA_OK : GQA_ERR_CUDA;
+}
+
+int fill_nan(void* o, const int64_t* os, const Shape& s, int dtype, cudaStream_t st) {
+  const int64_t n = (int64_t)s.batch * s.hq * s.seq_q * s.head_dim;
+  if (n == 0) return GQA_OK;
+  const uint16_t nan_bits = dtype == GQA_DTYPE_BF16 ? 0x7fc0 : 0x7e00;
+  const int blocks = (int)std::min<int64_t>((n + 255) / 256, 4096);
+  gqa_fill_nan_kernel<<<blocks, 256, 0, st>>>(reinterpret_cast<uint16_t*>(o), os[0], os[1], os[2], s.batch,
+                                              s.hq, s.seq_q, s.head_dim, nan_bits);
+  return launch_status();
+}
+
+int check_common(const void* q, const void* k, const void* v, const int64_t* qs, const int64_t* ks,
+                 const int64_t* vs, int dtype) {
+  if (dtype != GQA_DTYPE_BF16 && dtype != GQA_DTYPE_F16) return GQA_ERR_UNSUPPORTED;
+  int rc = check_strides(q, qs);
+  if (!rc) rc = check_strides(k, ks);
+  if (!rc) rc = check_strides(v, vs);
+  return rc;
+}
+
+}  // namespace
+}  // namespace gqa
+
+using namespace gqa;
+
+extern "C" {
+
+const char* gqa_strerror(int code) {
+  switch (code) {
+    case GQA_OK: return "success";
+    case GQA_ERR_INVALID_ARG: return "invalid argument (shape, null pointer or negative size)";
+    case GQA_ERR_UNSUPPORTED: return "unsupported configuration (head_dim must be 64 or 128, dtype f16/bf16, "
+                                     "num_heads/num_kv_heads a power of two <= 128)";
+    case GQA_ERR_ALIGNMENT: return "tensor must be contiguous in head_dim with 16-byte aligned base and strides";
+    case GQA_ERR_CUDA: return "CUDA runtime or driver call failed";
+    case GQA_ERR_TIMEOUT: return "bounded in-kernel wait expired (kernel aborted)";
+    case GQA_ERR_WORKSPACE: return "workspace missing or too small";
+    case GQA_ERR_NO_DEVICE: return "no sm_100 (B200) device is current";
+    default: return "unknown gqa status code";
+  }
+}
+
+int gqa_version(void) { return 100; }
+
+int gqa_sm_count(void) {
+  int sm = 0;
+  return current_device(&sm) == GQA_OK ? sm : 0;
+}
+
+size_t gqa_fwd_workspace_bytes(int batch, int num_heads, int num_kv_heads, int seq_q, int seq_kv, int head_dim) {
+  Shape s;
+  if (check_shape(batch, num_heads, num_kv_heads, seq_q, seq_kv, head_dim, &s)) return 0;
+  if (!use_stream(s) || seq_q == 0 || seq_kv == 0 || batch == 0) return 0;
+  int sm = 0;
+  if (current_device(&sm)) return 0;
+  const StreamPlan pl = plan_stream(s, sm, true);
+  return pl.nsplit > 1 ? stream_ws_bytes(pl, head_dim) : 0;
+}
+
+int gqa_fwd(const void* q, const void* k, const void* v, void* o, const int64_t* qs, const int64_t* ks,
+            const int64_t* vs, const int64_t* os, int batch, int num_heads, int num_kv_heads, int seq_q, int seq_kv,
+            int head_dim, float scale_log2, int causal, int dtype, void* workspace, size_t workspace_bytes,
+            void* stream) {
+  Shape s;
+  int rc = check_shape(batch, num_heads, num_kv_heads, seq_q, seq_kv, head_dim, &s);
+  if (rc) return rc;
+  if (batch == 0 || seq_q == 0) return GQA_OK;
+  rc = check_common(q, k, v, qs, ks, vs, dtype);
+  if (!rc) rc = check_strides(o, os);
+  if (rc) return rc;
+  int sm = 0;
+  rc = current_device(&sm);
+  if (rc) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (seq_kv == 0) return fill_nan(o, os, s, dtype, st);
+
+  if (use_stream(s)) {
+    StreamPlan pl = plan_stream(s, sm, true);
+    StreamParams p{};
+    p.q = reinterpret_cast<const uint16_t*>(q);
+    p.o = o;
+    p.q_sb = qs[0]; p.q_sh = qs[1]; p.q_sm = qs[2];
+    p.o_sb = os[0]; p.o_sh = os[1]; p.o_sm = os[2];
+    p.causal = causal ? 1 : 0;
+    p.scale_log2 = scale_log2;
+    p.kv_offset = 0;
+    p.seq_kv_total = seq_kv;
+    if (pl.nsplit > 1 && workspace && workspace_bytes >= stream_ws_bytes(pl, head_dim)) {
+      p.mode = kStreamFused;
+      stream_ws_carve(pl, head_dim, workspace, &p);
+    } else {
+      pl = plan_stream(s, sm, false);
+      p.mode = kStreamOut;
+    }
+    return run_stream(s, pl, p, k, v, ks, vs, dtype, st);
+  }
+
+  // tcgen05 prefill path
+  PrefillParams p{};
+  p.batch = batch;
+  p.hq = num_heads;
+  p.hkv = num_kv_heads;
+  p.group = s.group;
+  p.seq_q = seq_q;
+  p.seq_kv = seq_kv;
+  p.bm = 128 / s.group;
+  const int n_tiles = (seq_q + p.bm - 1) / p.bm;
+  p.n_pairs = (n_tiles + 1) / 2;
+  p.causal = causal ? 1 : 0;
+  p.scale_log2 = scale_log2;
+  CUtensorMap qm, km, vm, om;
+  rc = make_map(&qm, q, qs, batch, num_heads, seq_q, head_dim, p.bm, s.group);
+  if (!rc) rc = make_map(&km, k, ks, batch, num_kv_heads, seq_kv, head_dim, 128, 1);
+  if (!rc) rc = make_map(&vm, v, vs, batch, num_kv_heads, seq_kv, head_dim, 128, 1);
+  if (!rc) rc = make_map(&om, o, os, batch, num_heads, seq_q, head_dim, p.bm, s.group);
+  if (rc) return rc;
+  const int64_t grid = (int64_t)p.n_pairs * batch * num_kv_heads;
+  if (grid > 0x7fffffff) return GQA_ERR_INVALID_ARG;
+  const bool bf = dtype == GQA_DTYPE_BF16;
+  if (head_dim == 128) {
+    if (bf)
+      gqa_prefill_kernel<128, true><<<(unsigned)grid, PrefillCfg<128>::kThreads, PrefillCfg<128>::kSmemBytes, st>>>(p, qm, km, vm, om);
+    else
+      gqa_prefill_kernel<128, false><<<(unsigned)grid, PrefillCfg<128>::kThreads, PrefillCfg<128>::kSmemBytes, st>>>(p, qm, km, vm, om);
+  } else {
+    if (bf)
+      gqa_prefill_kernel<64, true><<<(unsigned)grid, PrefillCfg<128>::kThreads, PrefillCfg<64>::kSmemBytes, st>>>(p, qm, km, vm, om);
+    else
+      gqa_prefill_kernel<64, false><<<(unsigned)grid, PrefillCfg<128>::kThreads, PrefillCfg<64>::kSmemBytes, st>>>(p, qm, km, vm, om);
+  }
+  return launch_status();
+}
+
+int gqa_split_first(const void* q, const void* k, const void* v, float* m_p, float* l_p, float* acc_p,
+                    const int64_t* qs, const int64_t* ks, const int64_t* vs, const int64_t* ps, const int64_t* as,
+                    int batch, int num_heads, int num_kv_heads, int seq_q, int seq_kv, int head_dim,
+                    float scale_log2, int causal, int splits, int dtype, void* stream) {
+  Shape s;
+  int rc = check_shape(batch, num_heads, num_kv_heads, seq_q, seq_kv, head_dim, &s);
+  if (rc) return rc;
+  if (splits <= 0 || !m_p || !l_p || !acc_p || !ps || !as) return GQA_ERR_INVALID_ARG;
+  if (batch == 0 || seq_q == 0) return GQA_OK;
+  if (s.group > kStreamMaxRows) return GQA_ERR_UNSUPPORTED;
+  rc = check_common(q, k, v, qs, ks, vs, dtype);
+  if (rc) return rc;
+  int sm = 0;
+  rc = current_device(&sm);
+  if (rc) return rc;
+  if (seq_kv == 0) return GQA_ERR_INVALID_ARG;
+  StreamPlan pl = plan_stream(s, sm, false);
+  pl.nsplit = splits;
+  pl.chunk = (seq_kv + splits - 1) / splits;  // the reference's chunk size, tl.cdiv(seq_kv, SPLITS)
+  StreamParams p{};
+  p.q = reinterpret_cast<const uint16_t*>(q);
+  p.q_sb = qs[0]; p.q_sh = qs[1]; p.q_sm = qs[2];
+  p.causal = causal ? 1 : 0;
+  p.scale_log2 = scale_log2;
+  p.kv_offset = 0;
+  p.seq_kv_total = seq_kv;
+  p.mode = kStreamRefPartial;
+  p.m_p = m_p; p.l_p = l_p; p.acc_p = acc_p;
+  p.p_sb = ps[0]; p.p_sh = ps[1]; p.p_sm = ps[2]; p.p_ss = ps[3];
+  p.a_sb = as[0]; p.a_sh = as[1]; p.a_sm = as[2]; p.a_ss = as[3]; p.a_sd = as[4];
+  if ((int64_t)pl.units * splits > 0x7fffffff) return GQA_ERR_INVALID_ARG;
+  return run_stream(s, pl, p, k, v, ks, vs, dtype, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int gqa_split_reduce(const float* m_p, const float* l_p, const float* acc_p, void* o, const int64_t* ps,
+                     const int64_t* as, const int64_t* os, int batch, int num_heads, int seq_q, int head_dim,
+                     int splits, int dtype, void* stream) {
+  if (!m_p || !l_p || !acc_p || !o || !ps || !as || !os) return GQA_ERR_INVALID_ARG;
+  if (batch < 0 || num_heads <= 0 || seq_q < 0 || splits <= 0) return GQA_ERR_INVALID_ARG;
+  if (head_dim != 64 && head_dim != 128) return GQA_ERR_UNSUPPORTED;
+  if (dtype != GQA_DTYPE_BF16 && dtype != GQA_DTYPE_F16) return GQA_ERR_UNSUPPORTED;
+  if (os[3] != 1 || (reinterpret_cast<uintptr_t>(o) & 3u)) return GQA_ERR_ALIGNMENT;
+  for (int i = 0; i < 3; ++i)
+    if (os[i] % 2) return GQA_ERR_ALIGNMENT;
+  if (batch == 0 || seq_q == 0) return GQA_OK;
+  int rc = current_device(nullptr);
+  if (rc) return rc;
+  CombineParams p{};
+  p.m = m_p; p.l = l_p; p.acc = acc_p; p.o = o;
+  p.p_sb = ps[0]; p.p_sh = ps[1]; p.p_sm = ps[2]; p.p_ss = ps[3];
+  p.a_sb = as[0]; p.a_sh = as[1]; p.a_sm = as[2]; p.a_ss = as[3]; p.a_sd = as[4];
+  p.o_sb = os[0]; p.o_sh = os[1]; p.o_sm = os[2];
+  p.batch = batch; p.hq = num_heads; p.seq_q = seq_q; p.head_dim = head_dim; p.nsplit = splits;
+  const int64_t rows = (int64_t)batch * num_heads * seq_q;
+  const int64_t blocks = (rows + 3) / 4;
+  if (blocks > 0x7fffffff) return GQA_ERR_INVALID_ARG;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == GQA_DTYPE_BF16)
+    gqa_combine_kernel<true><<<(unsigned)blocks, 128, 0, st>>>(p);
+  else
+    gqa_combine_kernel<false><<<(unsigned)blocks, 128, 0, st>>>(p);
+  return launch_status();
+}
+
+size_t gqa_split_fused_workspace_bytes(int batch, int num_heads, int num_kv_heads, int seq_q, int seq_kv,
+                                       int head_dim) {
+  Shape s;
+  if (check_shape(batch, num_heads, num_kv_heads, seq_q, seq_kv, head_dim, &s)) return 0;
+  if (s.group > kStreamMaxRows || seq_q == 0 || seq_kv == 0 || batch == 0) return 0;
+  int sm = 0;
+  if (current_device(&sm)) return 0;
+  return stream_ws_bytes(plan_stream(s, sm, true), head_dim);
+}
+
+int gqa_split_fused(const void* q, const void* k, const void* v, void* o, const int64_t* qs, const int64_t* ks,
+                    const int64_t* vs, const int64_t* os, int batch, int num_heads, int num_kv_heads, int seq_q,
+                    int seq_kv, int head_dim, float scale_log2, int causal, int dtype, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  Shape s;
+  int rc = check_shape(batch, num_heads, num_kv_heads, seq_q, seq_kv, head_dim, &s);
+  if (rc) return rc;
+  if (batch == 0 || seq_q == 0) return GQA_OK;
+  if (s.group > kStreamMaxRows) return GQA_ERR_UNSUPPORTED;
+  rc = check_common(q, k, v, qs, ks, vs, dtype);
+  if (!rc) rc = check_strides(o, os);
+  if (rc) return rc;
+  int sm = 0;
+  rc = current_device(&sm);
+  if (rc) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (seq_kv == 0) return fill_nan(o, os, s, dtype, st);
+  const StreamPlan pl = plan_stream(s, sm, true);
+  if (!workspace || workspace_bytes < stream_ws_bytes(pl, head_dim) || !aligned16(workspace))
+    return GQA_ERR_WORKSPACE;
+  StreamParams p{};
+  p.q = reinterpret_cast<const uint16_t*>(q);
+  p.o = o;
+  p.q_sb = qs[0]; p.q_sh = qs[1]; p.q_sm = qs[2];
+  p.o_sb = os[0]; p.o_sh = os[1]; p.o_sm = os[2];
+  p.causal = causal ? 1 : 0;
+  p.scale_log2 = scale_log2;
+  p.kv_offset = 0;
+  p.seq_kv_total = seq_kv;
+  p.mode = kStreamFused;
+  stream_ws_carve(pl, head_dim, workspace, &p);
+  return run_stream(s, pl, p, k, v, ks, vs, dtype, st);
+}
+
+size_t gqa_partial_workspace_bytes(int batch, int num_heads, int num_kv_heads, int seq_q, int seq_kv_local,
+                                   int head_dim) {
+  Shape s;
+  if (check_shape(batch, num_heads, num_kv_heads, seq_q, seq_kv_local, head_dim, &s)) return 0;
+  if (s.group > kStreamMaxRows || seq_q == 0 || batch == 0) return 0;
+  int sm = 0;
+  if (current_device(&sm)) return 0;
+  return stream_ws_bytes(plan_stream(s, sm, true), head_dim);
+}
+
+int gqa_partial(const void* q, const void* k, const void* v, float* m_out, float* l_out, float* acc_out,
+                const int64_t* qs, const int64_t* ks, const int64_t* vs, int batch, int num_heads, int num_kv_heads,
+                int seq_q, int seq_kv_local, int kv_offset, int seq_kv_total, int head_dim, float scale_log2,
+                int causal, int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  Shape s;
+  int rc = check_shape(batch, num_heads, num_kv_heads, seq_q, seq_kv_local, head_dim, &s);
+  if (rc) return rc;
+  if (!m_out || !l_out || !acc_out) return GQA_ERR_INVALID_ARG;
+  if (kv_offset < 0 || seq_kv_total < kv_offset + seq_kv_local) return GQA_ERR_INVALID_ARG;
+  if (batch == 0 || seq_q == 0) return GQA_OK;
+  if (s.group > kStreamMaxRows) return GQA_ERR_UNSUPPORTED;
+  if (seq_kv_local == 0) return GQA_ERR_INVALID_ARG;
+  rc = check_common(q, k, v, qs, ks, vs, dtype);
+  if (rc) return rc;
+  if (!aligned16(acc_out)) return GQA_ERR_ALIGNMENT;
+  int sm = 0;
+  rc = current_device(&sm);
+  if (rc) return rc;
+  const StreamPlan pl = plan_stream(s, sm, true);
+  if (!workspace || workspace_bytes < stream_ws_bytes(pl, head_dim) || !aligned16(workspace))
+    return GQA_ERR_WORKSPACE;
+  StreamParams p{};
+  p.q = reinterpret_cast<const uint16_t*>(q);
+  p.q_sb = qs[0]; p.q_sh = qs[1]; p.q_sm = qs[2];
+  p.causal = causal ? 1 : 0;
+  p.scale_log2 = scale_log2;
+  p.kv_offset = kv_offset;
+  p.seq_kv_total = seq_kv_total;
+  p.mode = kStreamFusedPartial;
+  p.m_out = m_out; p.l_out = l_out; p.acc_out = acc_out;
+  stream_ws_carve(pl, head_dim, workspace, &p);
+  return run_stream(s, pl, p, k, v, ks, vs, dtype, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int gqa_lse_combine(const float* m_parts, const float* l_parts, const float* acc_parts, int nparts,
+                    int64_t ml_part_stride, int64_t acc_part_stride, void* o, const int64_t* os, int batch,
+                    int num_heads, int seq_q, int head_dim, int dtype, void* stream) {
+  if (nparts <= 0 || batch < 0 || seq_q < 0 || num_heads <= 0) return GQA_ERR_INVALID_ARG;
+  if (ml_part_stride < 0 || acc_part_stride < 0) return GQA_ERR_INVALID_ARG;
+  const int64_t ps[4] = {(int64_t)num_heads * seq_q, (int64_t)seq_q, 1, ml_part_stride};
+  const int64_t as[5] = {(int64_t)num_heads * seq_q * head_dim, (int64_t)seq_q * head_dim, (int64_t)head_dim,
+                         acc_part_stride, 1};
+  return gqa_split_reduce(m_parts, l_parts, acc_parts, o, ps, as, os, batch, num_heads, seq_q, head_dim, nparts,
+                          dtype, stream);
+}
+
+int gqa_device_error(int* code, int* site, int clear) {
+  int rc = current_device(nullptr);
+  if (rc) return rc;
+  int c = 0, s = 0;
+  if (cudaMemcpyFromSymbol(&c, g_device_error, sizeof(int)) != cudaSuccess) return GQA_ERR_CUDA;
+  if (cudaMemcpyFromSymbol(&s, g_device_error_site, sizeof(int)) != cudaSuccess) return GQA_ERR_CUDA;
+  if (code) *code = c;
+  if (site) *site = s;
+  if (clear) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)) != cudaSuccess) return GQA_ERR_CUDA;
+    if (cudaMemcpyToSymbol(g_device_error_site, &zero, sizeof(int)) != cudaSuccess) return GQA_ERR_CUDA;
+  }
+  return GQA_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,474 @@
+// HBM-streaming GQA attention kernel for few packed query rows (decode,
+// short chunked prefill). One CTA streams one chunk of the key axis of one
+// (batch, kv_head, q-block) unit through a TMA ring and keeps the online
+// softmax state of up to 64 packed rows (group_size heads x block_m positions)
+// in mma.sync accumulators. At <= 64 rows per 512 bytes of K+V the kernel is
+// bound by HBM bandwidth, not by the tensor pipe.
+//
+// Reference behaviour followed:
+//   gqa_kernels/gqa_split.py:46-112   per-chunk partial (m, l, acc), causal chunk clip
+//   gqa_kernels/gqa_split.py:134-147  log-sum-exp combine (fused here: last CTA per unit)
+//   gqa_kernels/gqa_fwd.py:57-73      group packing, bottom-right causal offset
+#pragma once
+
+#include "gqa_common.cuh"
+
+namespace gqa {
+
+enum StreamMode : int {
+  kStreamOut = 0,           // nsplit == 1: write O directly
+  kStreamRefPartial = 1,    // write (m, l, acc) at split index into caller arrays (reference layout)
+  kStreamFused = 2,         // write partial to workspace; last CTA of the unit combines into O
+  kStreamFusedPartial = 3,  // as kStreamFused, but the last CTA writes the combined (m, l, acc)
+};
+
+struct StreamParams {
+  const uint16_t* q;
+  void* o;
+  int64_t q_sb, q_sh, q_sm;  // element strides of Q (d stride is 1)
+  int64_t o_sb, o_sh, o_sm;
+  int batch, hq, hkv, group, seq_q, seq_kv;  // seq_kv: keys held by k/v (local shard)
+  int block_m;    // query positions per unit
+  int n_mtiles;   // ceil(seq_q / block_m)
+  int rows;       // group * block_m packed rows per unit (<= 16 * RG)
+  int nsplit;     // chunks per unit (gridDim.x = units * nsplit)
+  int chunk;      // keys per chunk
+  int causal;
+  float scale_log2;
+  int kv_offset;     // global position of local key 0
+  int seq_kv_total;  // global key count (causal offset = seq_kv_total - seq_q)
+  int mode;
+  // kStreamRefPartial outputs
+  float* m_p;
+  float* l_p;
+  float* acc_p;
+  int64_t p_sb, p_sh, p_sm, p_ss;
+  int64_t a_sb, a_sh, a_sm, a_ss, a_sd;
+  // kStreamFused / kStreamFusedPartial workspace
+  float* ws_m;    // [units][nsplit][rows]
+  float* ws_l;    // [units][nsplit][rows]
+  float* ws_acc;  // [units][nsplit][rows][HD]
+  unsigned* ws_cnt;  // [units] ticket counters, zero between calls
+  // kStreamFusedPartial outputs, contiguous (batch, hq, seq_q[, HD])
+  float* m_out;
+  float* l_out;
+  float* acc_out;
+};
+
+template <int HD>
+struct StreamCfg {
+  static constexpr int kBN = 64;                       // keys per stage
+  static constexpr int kNSub = HD / 64;                // 128-byte swizzle sub-tiles along d
+  static constexpr int kSubBytes = kBN * 128;          // one sub-tile: 64 keys x 128 B
+  static constexpr int kTileBytes = kNSub * kSubBytes;  // K (or V) stage
+  static constexpr int kStageBytes = 2 * kTileBytes;
+  static constexpr int kStages = (HD == 128) ? 3 : 6;
+  static constexpr int kRingBytes = kStages * kStageBytes;  // 96 KB
+  // barriers + flags after the ring
+  static constexpr int kSmemBytes = kRingBytes + 2 * kStages * 8 + 64 + 1024;
+  static constexpr int kThreads = 160;  // 4 compute warps + 1 TMA producer warp
+};
+
+template <int HD, bool BF16, int RG>
+__global__ void __launch_bounds__(160, 2)
+    gqa_stream_kernel(const StreamParams p, const __grid_constant__ CUtensorMap kmap,
+                      const __grid_constant__ CUtensorMap vmap) {
+  using Cfg = StreamCfg<HD>;
+  constexpr int KS = 4 / RG;        // warps sharing one row group split the stage's keys
+  constexpr int NKW = Cfg::kBN / KS;  // keys per warp per stage (16, 32, 64)
+  constexpr int NNB = NKW / 8;       // n8 blocks per warp per stage
+  constexpr int NDB = HD / 8;        // n8 blocks along d
+  constexpr int NKS = HD / 16;       // k16 steps along d
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_base = smem_u32(smem_raw);
+  const uint32_t base = (raw_base + 1023u) & ~1023u;
+  uint8_t* const smem = smem_raw + (base - raw_base);
+  const uint32_t bar_full = base + Cfg::kRingBytes;
+  const uint32_t bar_empty = bar_full + Cfg::kStages * 8;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kRingBytes + 2 * Cfg::kStages * 8);
+  int* last_flag = reinterpret_cast<int*>(smem + Cfg::kRingBytes + 2 * Cfg::kStages * 8 + 4);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+
+  // ---- work item -----------------------------------------------------------
+  const int split = blockIdx.x % p.nsplit;
+  const int unit = blockIdx.x / p.nsplit;
+  const int mt = unit % p.n_mtiles;
+  const int kvh = (unit / p.n_mtiles) % p.hkv;
+  const int b = unit / (p.n_mtiles * p.hkv);
+  const int off = p.seq_kv_total - p.seq_q;  // bottom-right causal offset (global)
+
+  // Highest key (local, exclusive) any valid row of this unit may see.
+  int kv_end = p.seq_kv;
+  if (p.causal) {
+    const int last_pos = min((mt + 1) * p.block_m, p.seq_q) - 1;
+    kv_end = min(kv_end, last_pos + off - p.kv_offset + 1);
+  }
+  const int k_begin = split * p.chunk;
+  const int k_end = min(k_begin + p.chunk, kv_end);
+  const int n_stages = (k_end > k_begin) ? (k_end - k_begin + Cfg::kBN - 1) / Cfg::kBN : 0;
+
+  if (tid == 0) {
+    for (int s = 0; s < Cfg::kStages; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, 4);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    fence_proxy_async_smem();
+  }
+  __syncthreads();
+
+  if (warp == 4) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0 && n_stages > 0) {
+      tma_prefetch_desc(&kmap);
+      tma_prefetch_desc(&vmap);
+      int t = 0;
+      for (; t < n_stages; ++t) {
+        const int slot = t % Cfg::kStages;
+        const int use = t / Cfg::kStages;
+        if (use > 0 && !mbar_wait(bar_empty + 8 * slot, (use - 1) & 1, abort_flag, 101)) break;
+        const uint32_t full = bar_full + 8 * slot;
+        mbar_arrive_expect_tx(full, Cfg::kStageBytes);
+        const int key0 = k_begin + t * Cfg::kBN;
+        const uint32_t kdst = base + slot * Cfg::kStageBytes;
+        const uint32_t vdst = kdst + Cfg::kTileBytes;
+#pragma unroll
+        for (int s = 0; s < Cfg::kNSub; ++s) {
+          tma_load_4d(kdst + s * Cfg::kSubBytes, &kmap, full, s * 64, key0, kvh, b);
+          tma_load_4d(vdst + s * Cfg::kSubBytes, &vmap, full, s * 64, key0, kvh, b);
+        }
+      }
+      // On abort, let the loads already issued land before the CTA exits.
+      if (t < n_stages) {
+        for (int u = max(0, t - Cfg::kStages); u < t; ++u) {
+          const int slot = u % Cfg::kStages;
+          volatile int dummy = 0;
+          mbar_wait(bar_full + 8 * slot, (u / Cfg::kStages) & 1, &dummy, 102);
+        }
+      }
+    }
+  } else {
+    // ----------------------------------------------------------------- compute
+    const int rg = warp % RG;
+    const int ks = warp / RG;
+    const int gr = lane >> 2;
+    const int gc = lane & 3;
+
+    // Packed rows owned by this thread: r0 = rg*16 + gr, r1 = r0 + 8.
+    int row_r[2];
+    bool valid_r[2];
+    int lim_r[2];  // local key limit (exclusive) for each row, clipped to the chunk
+    const uint16_t* qrow[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = rg * 16 + gr + 8 * h;
+      row_r[h] = r;
+      const int g = r / p.block_m;
+      const int m = r - g * p.block_m;
+      const int pos = mt * p.block_m + m;
+      valid_r[h] = (r < p.rows) && (pos < p.seq_q);
+      int lim = k_end;
+      if (p.causal) lim = min(lim, pos + off - p.kv_offset + 1);
+      lim_r[h] = lim;
+      qrow[h] = valid_r[h] ? p.q + b * p.q_sb + (int64_t)(kvh * p.group + g) * p.q_sh + (int64_t)pos * p.q_sm
+                           : nullptr;
+    }
+
+    // Q fragments (A operand, 16 rows x HD), loaded once.
+    uint32_t qa[NKS][4];
+#pragma unroll
+    for (int kk = 0; kk < NKS; ++kk) {
+      const int d0 = kk * 16 + gc * 2;
+      qa[kk][0] = qrow[0] ? *reinterpret_cast<const uint32_t*>(qrow[0] + d0) : 0u;
+      qa[kk][1] = qrow[1] ? *reinterpret_cast<const uint32_t*>(qrow[1] + d0) : 0u;
+      qa[kk][2] = qrow[0] ? *reinterpret_cast<const uint32_t*>(qrow[0] + d0 + 8) : 0u;
+      qa[kk][3] = qrow[1] ? *reinterpret_cast<const uint32_t*>(qrow[1] + d0 + 8) : 0u;
+    }
+
+    float acc[NDB][4];
+#pragma unroll
+    for (int i = 0; i < NDB; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+    float m_run[2] = {-INFINITY, -INFINITY};
+    float l_run[2] = {0.f, 0.f};
+    const float scale = p.scale_log2;
+
+    for (int t = 0; t < n_stages; ++t) {
+      const int slot = t % Cfg::kStages;
+      bool ok = mbar_wait(bar_full + 8 * slot, (t / Cfg::kStages) & 1, abort_flag, 103);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      const uint32_t kst = base + slot * Cfg::kStageBytes;
+      const uint32_t vst = kst + Cfg::kTileBytes;
+      const int key_w = k_begin + t * Cfg::kBN + ks * NKW;  // first key of this warp's block
+
+      // ---- S = Q K^T over this warp's NKW keys
+      float s[NNB][4];
+#pragma unroll
+      for (int nb = 0; nb < NNB; ++nb) s[nb][0] = s[nb][1] = s[nb][2] = s[nb][3] = 0.f;
+#pragma unroll
+      for (int kc = 0; kc < HD / 32; ++kc) {
+#pragma unroll
+        for (int nb = 0; nb < NNB; ++nb) {
+          const int krow = ks * NKW + nb * 8 + (lane & 7);
+          const int chunk = kc * 4 + (lane >> 3);
+          const uint32_t addr = kst + (chunk >> 3) * Cfg::kSubBytes + sw128_off(krow, chunk & 7);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(addr, b0, b1, b2, b3);
+          mma_16816<BF16>(s[nb], qa[2 * kc], b0, b1);
+          mma_16816<BF16>(s[nb], qa[2 * kc + 1], b2, b3);
+        }
+      }
+
+      // ---- online softmax (log2 domain)
+      float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+      for (int nb = 0; nb < NNB; ++nb) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int h = e >> 1;
+          const int key = key_w + nb * 8 + gc * 2 + (e & 1);
+          const float x = (key < lim_r[h]) ? s[nb][e] * scale : -INFINITY;
+          s[nb][e] = x;
+          mx[h] = fmaxf(mx[h], x);
+        }
+      }
+      float alpha[2], mu[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+        mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+        const float m_new = fmaxf(m_run[h], mx[h]);
+        mu[h] = (m_new == -INFINITY) ? 0.f : m_new;  // keeps fully-masked rows at p = 0, not NaN
+        alpha[h] = fast_exp2(m_run[h] - mu[h]);
+        m_run[h] = m_new;
+      }
+      float lsum[2] = {0.f, 0.f};
+#pragma unroll
+      for (int nb = 0; nb < NNB; ++nb) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float pv = fast_exp2(s[nb][e] - mu[e >> 1]);
+          s[nb][e] = pv;
+          lsum[e >> 1] += pv;
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) l_run[h] = l_run[h] * alpha[h] + lsum[h];
+#pragma unroll
+      for (int i = 0; i < NDB; ++i) {
+        acc[i][0] *= alpha[0];
+        acc[i][1] *= alpha[0];
+        acc[i][2] *= alpha[1];
+        acc[i][3] *= alpha[1];
+      }
+
+      // ---- O += P V
+#pragma unroll
+      for (int kk = 0; kk < NKW / 16; ++kk) {
+        uint32_t pa[4];
+        pa[0] = pack2<BF16>(s[2 * kk][0], s[2 * kk][1]);
+        pa[1] = pack2<BF16>(s[2 * kk][2], s[2 * kk][3]);
+        pa[2] = pack2<BF16>(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+        pa[3] = pack2<BF16>(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+        const int vrow = ks * NKW + kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+        for (int dc = 0; dc < NDB; dc += 2) {
+          const int chunk = dc + (lane >> 4);
+          const uint32_t addr = vst + (chunk >> 3) * Cfg::kSubBytes + sw128_off(vrow, chunk & 7);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(addr, b0, b1, b2, b3);
+          mma_16816<BF16>(acc[dc], pa, b0, b1);
+          mma_16816<BF16>(acc[dc + 1], pa, b2, b3);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_empty + 8 * slot);
+    }
+
+    // Row sums are per-thread partials over the quad's columns.
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 1);
+      l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 2);
+    }
+
+    // ---- merge the KS warps of each row group through shared memory
+    asm volatile("bar.sync 1, 128;" ::: "memory");  // every warp is done with the ring
+    float* mbuf = reinterpret_cast<float*>(smem);               // [4][16]
+    float* lbuf = mbuf + 64;                                    // [4][16]
+    float* abuf = lbuf + 64;                                    // [4][16][HD]
+    {
+      float* aw = abuf + warp * 16 * HD;
+#pragma unroll
+      for (int i = 0; i < NDB; ++i) {
+        const int d = i * 8 + gc * 2;
+        *reinterpret_cast<float2*>(aw + gr * HD + d) = make_float2(acc[i][0], acc[i][1]);
+        *reinterpret_cast<float2*>(aw + (gr + 8) * HD + d) = make_float2(acc[i][2], acc[i][3]);
+      }
+      if (gc == 0) {
+        mbuf[warp * 16 + gr] = m_run[0];
+        mbuf[warp * 16 + gr + 8] = m_run[1];
+        lbuf[warp * 16 + gr] = l_run[0];
+        lbuf[warp * 16 + gr + 8] = l_run[1];
+      }
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+
+    // Combined per-row (M, L) for the rows of this CTA -> fin buffers.
+    float* fin_m = abuf + 4 * 16 * HD;  // [64]
+    float* fin_l = fin_m + 64;          // [64]
+    float* fin_w = fin_l + 64;          // [64][4] per-warp weights
+    if (tid < RG * 16) {
+      const int r = tid;
+      const int g_rg = r / 16, rr = r % 16;
+      float M = -INFINITY;
+#pragma unroll
+      for (int k2 = 0; k2 < KS; ++k2) M = fmaxf(M, mbuf[(k2 * RG + g_rg) * 16 + rr]);
+      const float Mu = (M == -INFINITY) ? 0.f : M;
+      float L = 0.f;
+#pragma unroll
+      for (int k2 = 0; k2 < KS; ++k2) {
+        const int w = k2 * RG + g_rg;
+        const float wt = fast_exp2(mbuf[w * 16 + rr] - Mu);
+        fin_w[r * 4 + k2] = wt;
+        L += wt * lbuf[w * 16 + rr];
+      }
+      fin_m[r] = M;
+      fin_l[r] = L;
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+
+    // Cooperative pass over (row, 4 consecutive d): combined acc -> destination.
+    const int n_rows = min(p.rows, RG * 16);
+    const int per_row = HD / 4;
+    if (p.mode == kStreamOut) {
+      for (int idx = tid; idx < n_rows * per_row; idx += 128) {
+        const int r = idx / per_row, d = (idx - r * per_row) * 4;
+        const int g = r / p.block_m, m = r - g * p.block_m, pos = mt * p.block_m + m;
+        if (pos >= p.seq_q) continue;
+        const int g_rg = r / 16, rr = r % 16;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int k2 = 0; k2 < KS; ++k2) {
+          const float wt = fin_w[r * 4 + k2];
+          const float4 v = *reinterpret_cast<const float4*>(abuf + ((k2 * RG + g_rg) * 16 + rr) * HD + d);
+          a.x += wt * v.x; a.y += wt * v.y; a.z += wt * v.z; a.w += wt * v.w;
+        }
+        const float inv = 1.f / fin_l[r];  // l == 0 (no visible key) -> NaN, as the reference
+        uint2 pk;
+        pk.x = pack2<BF16>(a.x * inv, a.y * inv);
+        pk.y = pack2<BF16>(a.z * inv, a.w * inv);
+        uint16_t* dst = reinterpret_cast<uint16_t*>(p.o) + b * p.o_sb + (int64_t)(kvh * p.group + g) * p.o_sh +
+                        (int64_t)pos * p.o_sm + d;
+        *reinterpret_cast<uint2*>(dst) = pk;
+      }
+    } else if (p.mode == kStreamRefPartial) {
+      for (int idx = tid; idx < n_rows * per_row; idx += 128) {
+        const int r = idx / per_row, d = (idx - r * per_row) * 4;
+        const int g = r / p.block_m, m = r - g * p.block_m, pos = mt * p.block_m + m;
+        if (pos >= p.seq_q) continue;
+        const int g_rg = r / 16, rr = r % 16;
+        const int head = kvh * p.group + g;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int k2 = 0; k2 < KS; ++k2) {
+          const float wt = fin_w[r * 4 + k2];
+          const float4 v = *reinterpret_cast<const float4*>(abuf + ((k2 * RG + g_rg) * 16 + rr) * HD + d);
+          a.x += wt * v.x; a.y += wt * v.y; a.z += wt * v.z; a.w += wt * v.w;
+        }
+        float* ap = p.acc_p + b * p.a_sb + head * p.a_sh + (int64_t)pos * p.a_sm + (int64_t)split * p.a_ss;
+        ap[(int64_t)(d + 0) * p.a_sd] = a.x;
+        ap[(int64_t)(d + 1) * p.a_sd] = a.y;
+        ap[(int64_t)(d + 2) * p.a_sd] = a.z;
+        ap[(int64_t)(d + 3) * p.a_sd] = a.w;
+        if (d == 0) {
+          const int64_t po = b * p.p_sb + head * p.p_sh + (int64_t)pos * p.p_sm + (int64_t)split * p.p_ss;
+          p.m_p[po] = fin_m[r];
+          p.l_p[po] = fin_l[r];
+        }
+      }
+    } else {
+      // kStreamFused / kStreamFusedPartial: publish this chunk's partial.
+      const int64_t wbase = ((int64_t)unit * p.nsplit + split) * p.rows;
+      for (int idx = tid; idx < n_rows * per_row; idx += 128) {
+        const int r = idx / per_row, d = (idx - r * per_row) * 4;
+        const int g_rg = r / 16, rr = r % 16;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int k2 = 0; k2 < KS; ++k2) {
+          const float wt = fin_w[r * 4 + k2];
+          const float4 v = *reinterpret_cast<const float4*>(abuf + ((k2 * RG + g_rg) * 16 + rr) * HD + d);
+          a.x += wt * v.x; a.y += wt * v.y; a.z += wt * v.z; a.w += wt * v.w;
+        }
+        __stcg(reinterpret_cast<float4*>(p.ws_acc + (wbase + r) * HD + d), a);
+        if (d == 0) {
+          __stcg(p.ws_m + wbase + r, fin_m[r]);
+          __stcg(p.ws_l + wbase + r, fin_l[r]);
+        }
+      }
+      __threadfence();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (tid == 0) {
+        const unsigned ticket = atomicAdd(p.ws_cnt + unit, 1u);
+        *last_flag = (ticket == (unsigned)(p.nsplit - 1)) ? 1 : 0;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (*last_flag) {
+        __threadfence();
+        // Per-row weights over the unit's chunks: w_s = exp2(m_s - max_s m_s).
+        float* wsm = fin_w + 64 * 4;  // [rows][nsplit], rows * nsplit <= 4096 (host-enforced)
+        const int64_t ubase = (int64_t)unit * p.nsplit * p.rows;
+        for (int r = tid; r < n_rows; r += 128) {
+          float M = -INFINITY;
+          for (int s2 = 0; s2 < p.nsplit; ++s2) M = fmaxf(M, __ldcg(p.ws_m + ubase + (int64_t)s2 * p.rows + r));
+          const float Mu = (M == -INFINITY) ? 0.f : M;
+          float L = 0.f;
+          for (int s2 = 0; s2 < p.nsplit; ++s2) {
+            const float wt = fast_exp2(__ldcg(p.ws_m + ubase + (int64_t)s2 * p.rows + r) - Mu);
+            wsm[r * p.nsplit + s2] = wt;
+            L += wt * __ldcg(p.ws_l + ubase + (int64_t)s2 * p.rows + r);
+          }
+          fin_m[r] = M;
+          fin_l[r] = L;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        for (int idx = tid; idx < n_rows * per_row; idx += 128) {
+          const int r = idx / per_row, d = (idx - r * per_row) * 4;
+          const int g = r / p.block_m, m = r - g * p.block_m, pos = mt * p.block_m + m;
+          if (pos >= p.seq_q) continue;
+          float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int s2 = 0; s2 < p.nsplit; ++s2) {
+            const float wt = wsm[r * p.nsplit + s2];
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(p.ws_acc + (ubase + (int64_t)s2 * p.rows + r) * HD + d));
+            a.x += wt * v.x; a.y += wt * v.y; a.z += wt * v.z; a.w += wt * v.w;
+          }
+          const int head = kvh * p.group + g;
+          if (p.mode == kStreamFused) {
+            const float inv = 1.f / fin_l[r];
+            uint2 pk;
+            pk.x = pack2<BF16>(a.x * inv, a.y * inv);
+            pk.y = pack2<BF16>(a.z * inv, a.w * inv);
+            uint16_t* dst = reinterpret_cast<uint16_t*>(p.o) + b * p.o_sb + (int64_t)head * p.o_sh +
+                            (int64_t)pos * p.o_sm + d;
+            *reinterpret_cast<uint2*>(dst) = pk;
+          } else {
+            const int64_t ro = ((int64_t)b * p.hq + head) * p.seq_q + pos;
+            *reinterpret_cast<float4*>(p.acc_out + ro * HD + d) = a;
+            if (d == 0) {
+              p.m_out[ro] = fin_m[r];
+              p.l_out[ro] = fin_l[r];
+            }
+          }
+        }
+        if (tid == 0) p.ws_cnt[unit] = 0u;  // ready for the next call on this workspace
+      }
+    }
+  }
+}
+
+}  // namespace gqa

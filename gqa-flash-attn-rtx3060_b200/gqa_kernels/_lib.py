@@ -1,0 +1,147 @@
+"""ctypes binding of libgqa_sm100.so, the sm_100a CUDA library behind gqa_kernels.
+
+This is the Python-side FFI of the C ABI declared in include/gqa_sm100.h.
+There is no fallback: if the library is missing or the current device is not
+an sm_100 GPU, calls raise RuntimeError.
+"""
+import ctypes
+import os
+import threading
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libgqa_sm100.so")
+
+GQA_DTYPE_F16 = 0
+GQA_DTYPE_BF16 = 1
+
+_P = ctypes.c_void_p
+_I64P = ctypes.POINTER(ctypes.c_int64)
+_I = ctypes.c_int
+_F = ctypes.c_float
+_SZ = ctypes.c_size_t
+
+# name -> (restype, argtypes); mirrors include/gqa_sm100.h
+SIGNATURES = {
+    "gqa_strerror": (ctypes.c_char_p, [_I]),
+    "gqa_version": (_I, []),
+    "gqa_sm_count": (_I, []),
+    "gqa_fwd_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I, _I]),
+    "gqa_fwd": (_I, [_P, _P, _P, _P, _I64P, _I64P, _I64P, _I64P, _I, _I, _I, _I, _I, _I, _F, _I, _I, _P, _SZ, _P]),
+    "gqa_split_first": (_I, [_P, _P, _P, _P, _P, _P, _I64P, _I64P, _I64P, _I64P, _I64P,
+                             _I, _I, _I, _I, _I, _I, _F, _I, _I, _I, _P]),
+    "gqa_split_reduce": (_I, [_P, _P, _P, _P, _I64P, _I64P, _I64P, _I, _I, _I, _I, _I, _I, _P]),
+    "gqa_split_fused_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I, _I]),
+    "gqa_split_fused": (_I, [_P, _P, _P, _P, _I64P, _I64P, _I64P, _I64P, _I, _I, _I, _I, _I, _I, _F, _I, _I,
+                             _P, _SZ, _P]),
+    "gqa_partial_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I, _I]),
+    "gqa_partial": (_I, [_P, _P, _P, _P, _P, _P, _I64P, _I64P, _I64P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _I, _I,
+                         _P, _SZ, _P]),
+    "gqa_lse_combine": (_I, [_P, _P, _P, _I, ctypes.c_int64, ctypes.c_int64, _P, _I64P, _I, _I, _I, _I, _I, _P]),
+    "gqa_device_error": (_I, [ctypes.POINTER(_I), ctypes.POINTER(_I), _I]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load():
+    """Loads (once) and returns the ctypes handle of libgqa_sm100.so."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise RuntimeError(
+                        f"{LIB_PATH} is missing: build it with "
+                        "`python gqa-flash-attn-rtx3060_b200/build.py` (nvcc, sm_100a)")
+                lib = ctypes.CDLL(LIB_PATH)
+                for name, (res, args) in SIGNATURES.items():
+                    fn = getattr(lib, name)
+                    fn.restype = res
+                    fn.argtypes = args
+                _lib = lib
+    return _lib
+
+
+def strerror(code):
+    return load().gqa_strerror(int(code)).decode()
+
+
+def check(code, what):
+    if code != 0:
+        raise RuntimeError(f"{what} failed: {strerror(code)} (status {code})")
+
+
+def strides(t, n=4):
+    """Element strides of `t` as a ctypes int64 array."""
+    return (ctypes.c_int64 * n)(*t.stride())
+
+
+def dtype_code(t):
+    if t.dtype == torch.bfloat16:
+        return GQA_DTYPE_BF16
+    if t.dtype == torch.float16:
+        return GQA_DTYPE_F16
+    raise RuntimeError(f"gqa_kernels supports float16 and bfloat16 tensors, got {t.dtype}")
+
+
+def stream_ptr(device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def tma_compatible(t):
+    """True if `t` meets the library's layout rule: contiguous in the last dim,
+    other strides multiples of 8 elements, base 16-byte aligned."""
+    if t.stride(-1) != 1 and t.shape[-1] != 1:
+        return False
+    if t.data_ptr() % 16:
+        return False
+    return all(s % 8 == 0 for s in t.stride()[:-1])
+
+
+class WorkspaceCache:
+    """Per-(device, stream) scratch for the split kernels.
+
+    The fused kernels count chunk arrivals with ticket counters that must read
+    zero at the start of a call and are reset to zero by the call itself. A
+    buffer is zeroed when it is (re)allocated or when the call signature
+    changes (a different shape moves the counters), so steady-state calls
+    launch no memset. Calls sharing a stream are ordered, so they may share
+    its buffer.
+    """
+
+    def __init__(self):
+        self._bufs = {}
+        self._lock = threading.Lock()
+
+    def get(self, device, nbytes, signature):
+        stream = torch.cuda.current_stream(device)
+        key = (device.index, stream.cuda_stream)
+        with self._lock:
+            ent = self._bufs.get(key)
+            if ent is None or ent[0].numel() < nbytes:
+                buf = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
+                self._bufs[key] = [buf, signature]
+                return buf
+            if ent[1] != signature:
+                ent[0].zero_()
+                ent[1] = signature
+            return ent[0]
+
+    def drop(self, device):
+        with self._lock:
+            for key in [k for k in self._bufs if k[0] == device.index]:
+                del self._bufs[key]
+
+
+WORKSPACES = WorkspaceCache()
+
+
+def device_error(clear=True):
+    """Returns (code, site) of the current device's in-kernel error word."""
+    code = ctypes.c_int(0)
+    site = ctypes.c_int(0)
+    check(load().gqa_device_error(ctypes.byref(code), ctypes.byref(site), 1 if clear else 0), "gqa_device_error")
+    return code.value, site.value

@@ -1,0 +1,155 @@
+/*
+ * gqa_sm100.h -- C ABI of libgqa_sm100.so, the B200 (sm_100a) GQA
+ * flash-attention forward.
+ *
+ * Conventions shared by every entry point:
+ *   - All pointers are device pointers owned by the caller; the library never
+ *     allocates device memory. Kernels that need scratch take a caller-owned
+ *     workspace (see *_workspace_bytes).
+ *   - Tensors use the reference layout: Q/O (batch, num_heads, seq_q, head_dim),
+ *     K/V (batch, num_kv_heads, seq_kv, head_dim). Strides are in ELEMENTS, in
+ *     dimension order (b, h, s, d). The d stride must be 1 and every other
+ *     stride a multiple of 8 elements (16 bytes); base pointers 16-byte aligned.
+ *   - dtype: GQA_DTYPE_F16 or GQA_DTYPE_BF16 (q, k, v and o share it).
+ *   - scale_log2 = head_dim^-0.5 * log2(e); the softmax is evaluated with exp2.
+ *   - causal = 1: query row i (in key coordinates i + seq_kv - seq_q) attends
+ *     to keys [0, i + seq_kv - seq_q] (bottom-right alignment). A row with no
+ *     visible key produces NaN, as the reference does.
+ *   - Work is enqueued on `stream` (a cudaStream_t; NULL = legacy default);
+ *     no entry point synchronises. Return 0 on success or a GQA_ERR_* code;
+ *     gqa_strerror() turns a code into text.
+ *   - Entry points are stateless and re-entrant; per-device attributes are
+ *     cached once under a mutex.
+ */
+#ifndef GQA_SM100_H_
+#define GQA_SM100_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GQA_OK 0
+#define GQA_ERR_INVALID_ARG 1   /* bad shape, null pointer, negative size      */
+#define GQA_ERR_UNSUPPORTED 2   /* head_dim not 64/128, group size not 2^k ... */
+#define GQA_ERR_ALIGNMENT 3     /* stride or base pointer not 16-byte aligned  */
+#define GQA_ERR_CUDA 4          /* a CUDA runtime/driver call failed           */
+#define GQA_ERR_TIMEOUT 5       /* a bounded in-kernel wait expired            */
+#define GQA_ERR_WORKSPACE 6     /* workspace missing or too small              */
+#define GQA_ERR_NO_DEVICE 7     /* no sm_100 device current                    */
+
+#define GQA_DTYPE_F16 0
+#define GQA_DTYPE_BF16 1
+
+/* Text for a status code (static storage). */
+const char* gqa_strerror(int code);
+
+/* Library version, major*10000 + minor*100 + patch (0.1.0 -> 100). */
+int gqa_version(void);
+
+/*
+ * Single-pass GQA forward: O = softmax(Q K^T * scale) V with the group's
+ * query heads packed into the M dimension of each tile.
+ * Replaces the launch of gqa_fwd_kernel in gqa_kernels/dispatch.py:50-61
+ * (kernel body gqa_kernels/gqa_fwd.py:33-109).
+ * Packed rows (group_size * seq_q) >= 128 run the tcgen05/TMEM prefill
+ * kernel; fewer run the HBM-streaming kernel, which may split the key range
+ * across CTAs when `workspace` is large enough
+ * (gqa_fwd_workspace_bytes) -- the combine is fused into the same launch.
+ */
+size_t gqa_fwd_workspace_bytes(int batch, int num_heads, int num_kv_heads, int seq_q, int seq_kv,
+                               int head_dim);
+int gqa_fwd(const void* q, const void* k, const void* v, void* o, const int64_t* q_strides4,
+            const int64_t* k_strides4, const int64_t* v_strides4, const int64_t* o_strides4, int batch,
+            int num_heads, int num_kv_heads, int seq_q, int seq_kv, int head_dim, float scale_log2,
+            int causal, int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Split-KV first pass: per-(row, split) partial softmax statistics over key
+ * chunk [s*ceil(seq_kv/splits), min((s+1)*ceil(seq_kv/splits), seq_kv)).
+ * m_p, l_p: float32 (batch, num_heads, seq_q, splits) with strides p_strides4;
+ * acc_p: float32 (batch, num_heads, seq_q, splits, head_dim), strides a_strides5.
+ * m is in log2 units (already multiplied by scale_log2), l = sum exp2(s - m),
+ * acc = sum exp2(s - m) v (unnormalised). An empty chunk gives (-inf, 0, 0).
+ * Replaces gqa_split_first_kernel, gqa_kernels/gqa_split.py:26-112, launched at :168-183.
+ */
+int gqa_split_first(const void* q, const void* k, const void* v, float* m_p, float* l_p, float* acc_p,
+                    const int64_t* q_strides4, const int64_t* k_strides4, const int64_t* v_strides4,
+                    const int64_t* p_strides4, const int64_t* a_strides5, int batch, int num_heads,
+                    int num_kv_heads, int seq_q, int seq_kv, int head_dim, float scale_log2, int causal,
+                    int splits, int dtype, void* stream);
+
+/*
+ * Split-KV second pass: log-sum-exp combine of the partials above into O.
+ * Replaces gqa_split_reduce_kernel, gqa_kernels/gqa_split.py:115-147, launched at :185-193.
+ */
+int gqa_split_reduce(const float* m_p, const float* l_p, const float* acc_p, void* o,
+                     const int64_t* p_strides4, const int64_t* a_strides5, const int64_t* o_strides4,
+                     int batch, int num_heads, int seq_q, int head_dim, int splits, int dtype, void* stream);
+
+/*
+ * One-launch split-KV forward: the key range is split into chunks sized for
+ * the device's SM count and the last CTA of each (batch, kv_head, q-block)
+ * combines the chunk partials in-kernel (atomic ticket, no second launch).
+ * Same result as split_kv_forward, gqa_kernels/gqa_split.py:153-194.
+ * The workspace must hold gqa_split_fused_workspace_bytes() bytes and its
+ * ticket counters must be zero before the first call; every call leaves them
+ * zero again. Calls sharing a workspace must be ordered on one stream.
+ */
+size_t gqa_split_fused_workspace_bytes(int batch, int num_heads, int num_kv_heads, int seq_q, int seq_kv,
+                                       int head_dim);
+int gqa_split_fused(const void* q, const void* k, const void* v, void* o, const int64_t* q_strides4,
+                    const int64_t* k_strides4, const int64_t* v_strides4, const int64_t* o_strides4,
+                    int batch, int num_heads, int num_kv_heads, int seq_q, int seq_kv, int head_dim,
+                    float scale_log2, int causal, int dtype, void* workspace, size_t workspace_bytes,
+                    void* stream);
+
+/*
+ * Partial attention over one shard of the key axis, for a key range split
+ * across GPUs. k and v hold keys [kv_offset, kv_offset + seq_kv_local) of a
+ * sequence of seq_kv_total keys; causal masking uses global key positions.
+ * Outputs are float32, contiguous: m_out/l_out (batch, num_heads, seq_q),
+ * acc_out (batch, num_heads, seq_q, head_dim), with the meaning of
+ * gqa_split_first's (m, l, acc) for this shard.
+ * No reference counterpart (the reference is single-GPU); the partial
+ * definition follows gqa_kernels/gqa_split.py:102-112.
+ */
+size_t gqa_partial_workspace_bytes(int batch, int num_heads, int num_kv_heads, int seq_q, int seq_kv_local,
+                                   int head_dim);
+int gqa_partial(const void* q, const void* k, const void* v, float* m_out, float* l_out, float* acc_out,
+                const int64_t* q_strides4, const int64_t* k_strides4, const int64_t* v_strides4, int batch,
+                int num_heads, int num_kv_heads, int seq_q, int seq_kv_local, int kv_offset, int seq_kv_total,
+                int head_dim, float scale_log2, int causal, int dtype, void* workspace, size_t workspace_bytes,
+                void* stream);
+
+/*
+ * Log-sum-exp combine of `nparts` partial sets (e.g. one per GPU). Part s
+ * holds, for row r = (b*num_heads + h)*seq_q + i, the values
+ * m_parts[s*ml_part_stride + r], l_parts[s*ml_part_stride + r] and
+ * acc_parts[s*acc_part_stride + r*head_dim + d] (float32), i.e. gqa_partial's
+ * outputs stacked along a leading axis -- either as three stacked arrays or as
+ * one packed [m | l | acc] buffer per part, as an all-gather produces.
+ * Algebra of gqa_kernels/gqa_split.py:137-144, applied across parts.
+ */
+int gqa_lse_combine(const float* m_parts, const float* l_parts, const float* acc_parts, int nparts,
+                    int64_t ml_part_stride, int64_t acc_part_stride, void* o, const int64_t* o_strides4, int batch,
+                    int num_heads, int seq_q, int head_dim, int dtype, void* stream);
+
+/*
+ * Reads (and clears, if `clear` is nonzero) the device error word of the
+ * current device: 0, or GQA_ERR_TIMEOUT when a bounded in-kernel wait expired.
+ * `site` (optional) receives the wait site id. Synchronises the current device.
+ * No reference counterpart (the reference has no in-kernel waits).
+ */
+int gqa_device_error(int* code, int* site, int clear);
+
+/* Number of SMs of the current device as used for split sizing. */
+int gqa_sm_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GQA_SM100_H_ */
