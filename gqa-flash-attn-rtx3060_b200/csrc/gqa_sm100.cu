@@ -320,14 +320,17 @@ int gqa_fwd(const void* q, const void* k, const void* v, void* o, const int64_t*
   int rc = check_shape(batch, num_heads, num_kv_heads, seq_q, seq_kv, head_dim, &s);
   if (rc) return rc;
   if (batch == 0 || seq_q == 0) return GQA_OK;
-  rc = check_common(q, k, v, qs, ks, vs, dtype);
-  if (!rc) rc = check_strides(o, os);
+  if (dtype != GQA_DTYPE_BF16 && dtype != GQA_DTYPE_F16) return GQA_ERR_UNSUPPORTED;
+  rc = check_strides(o, os);
   if (rc) return rc;
   int sm = 0;
   rc = current_device(&sm);
   if (rc) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // No key at all (k and v may have no storage): every row sees nothing -> NaN.
   if (seq_kv == 0) return fill_nan(o, os, s, dtype, st);
+  rc = check_common(q, k, v, qs, ks, vs, dtype);
+  if (rc) return rc;
 
   if (use_stream(s)) {
     StreamPlan pl = plan_stream(s, sm, true);
@@ -469,14 +472,16 @@ int gqa_split_fused(const void* q, const void* k, const void* v, void* o, const 
   if (rc) return rc;
   if (batch == 0 || seq_q == 0) return GQA_OK;
   if (s.group > kStreamMaxRows) return GQA_ERR_UNSUPPORTED;
-  rc = check_common(q, k, v, qs, ks, vs, dtype);
-  if (!rc) rc = check_strides(o, os);
+  if (dtype != GQA_DTYPE_BF16 && dtype != GQA_DTYPE_F16) return GQA_ERR_UNSUPPORTED;
+  rc = check_strides(o, os);
   if (rc) return rc;
   int sm = 0;
   rc = current_device(&sm);
   if (rc) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (seq_kv == 0) return fill_nan(o, os, s, dtype, st);
+  rc = check_common(q, k, v, qs, ks, vs, dtype);
+  if (rc) return rc;
   const StreamPlan pl = plan_stream(s, sm, true);
   if (!workspace || workspace_bytes < stream_ws_bytes(pl, head_dim) || !aligned16(workspace))
     return GQA_ERR_WORKSPACE;
