@@ -291,6 +291,8 @@ const char* gqa_strerror(int code) {
     case GQA_ERR_TIMEOUT: return "bounded in-kernel wait expired (kernel aborted)";
     case GQA_ERR_WORKSPACE: return "workspace missing or too small";
     case GQA_ERR_NO_DEVICE: return "no sm_100 (B200) device is current";
+    case GQA_ERR_SCRATCH_LIMIT: return "problem needs more scratch than the static no-allocation buffer "
+                                       "(GQA_NOALLOC_SCRATCH_BYTES) holds";
     default: return "unknown gqa status code";
   }
 }
@@ -496,6 +498,77 @@ int gqa_split_fused(const void* q, const void* k, const void* v, void* o, const 
   p.seq_kv_total = seq_kv;
   p.mode = kStreamFused;
   stream_ws_carve(pl, head_dim, workspace, &p);
+  return run_stream(s, pl, p, k, v, ks, vs, dtype, st);
+}
+
+}  // extern "C"
+
+// ----------------------------------------------------------------------------- no-allocation variant
+// Scratch of gqa_split_fused_noalloc. Host code must not pass the symbol itself
+// to a kernel (in host code it names a host-side stand-in); its device address
+// comes from cudaGetSymbolAddress, looked up once per device.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[GQA_NOALLOC_SCRATCH_BYTES];
+
+namespace gqa {
+namespace {
+std::vector<void*> g_noalloc_addr;  // per device, guarded by g_mutex
+
+int noalloc_scratch_address(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return GQA_ERR_NO_DEVICE;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if ((int)g_noalloc_addr.size() <= dev) g_noalloc_addr.resize(dev + 1, nullptr);
+  if (!g_noalloc_addr[dev]) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) return GQA_ERR_CUDA;
+    g_noalloc_addr[dev] = ptr;
+  }
+  *out = g_noalloc_addr[dev];
+  return GQA_OK;
+}
+}  // namespace
+}  // namespace gqa
+
+extern "C" {
+
+int gqa_split_fused_noalloc(const void* q, const void* k, const void* v, void* o, const int64_t* qs,
+                            const int64_t* ks, const int64_t* vs, const int64_t* os, int batch, int num_heads,
+                            int num_kv_heads, int seq_q, int seq_kv, int head_dim, float scale_log2, int causal,
+                            int dtype, void* stream) {
+  Shape s;
+  int rc = check_shape(batch, num_heads, num_kv_heads, seq_q, seq_kv, head_dim, &s);
+  if (rc) return rc;
+  if (batch == 0 || seq_q == 0) return GQA_OK;
+  if (s.group > kStreamMaxRows) return GQA_ERR_UNSUPPORTED;
+  if (dtype != GQA_DTYPE_BF16 && dtype != GQA_DTYPE_F16) return GQA_ERR_UNSUPPORTED;
+  rc = check_strides(o, os);
+  if (rc) return rc;
+  int sm = 0;
+  rc = current_device(&sm);
+  if (rc) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (seq_kv == 0) return fill_nan(o, os, s, dtype, st);
+  rc = check_common(q, k, v, qs, ks, vs, dtype);
+  if (rc) return rc;
+  const StreamPlan pl = plan_stream(s, sm, true);
+  if (stream_ws_bytes(pl, head_dim) > (size_t)GQA_NOALLOC_SCRATCH_BYTES) return GQA_ERR_SCRATCH_LIMIT;
+  void* scratch = nullptr;
+  rc = noalloc_scratch_address(&scratch);
+  if (rc) return rc;
+  StreamParams p{};
+  p.q = reinterpret_cast<const uint16_t*>(q);
+  p.o = o;
+  p.q_sb = qs[0]; p.q_sh = qs[1]; p.q_sm = qs[2];
+  p.o_sb = os[0]; p.o_sh = os[1]; p.o_sm = os[2];
+  p.causal = causal ? 1 : 0;
+  p.scale_log2 = scale_log2;
+  p.kv_offset = 0;
+  p.seq_kv_total = seq_kv;
+  p.mode = kStreamFused;
+  stream_ws_carve(pl, head_dim, scratch, &p);
+  // The array keeps the previous call's contents, possibly laid out for another
+  // shape: the ticket counters must read zero, so clear them on this stream.
+  if (cudaMemsetAsync(p.ws_cnt, 0, (size_t)pl.units * sizeof(unsigned), st) != cudaSuccess) return GQA_ERR_CUDA;
   return run_stream(s, pl, p, k, v, ks, vs, dtype, st);
 }
 

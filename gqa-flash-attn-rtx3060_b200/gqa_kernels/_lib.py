@@ -35,6 +35,8 @@ SIGNATURES = {
     "gqa_split_fused_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I, _I]),
     "gqa_split_fused": (_I, [_P, _P, _P, _P, _I64P, _I64P, _I64P, _I64P, _I, _I, _I, _I, _I, _I, _F, _I, _I,
                              _P, _SZ, _P]),
+    "gqa_split_fused_noalloc": (_I, [_P, _P, _P, _P, _I64P, _I64P, _I64P, _I64P, _I, _I, _I, _I, _I, _I, _F, _I, _I,
+                                     _P]),
     "gqa_partial_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I, _I]),
     "gqa_partial": (_I, [_P, _P, _P, _P, _P, _P, _I64P, _I64P, _I64P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _I, _I,
                          _P, _SZ, _P]),

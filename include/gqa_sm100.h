@@ -39,6 +39,7 @@ extern "C" {
 #define GQA_ERR_TIMEOUT 5       /* a bounded in-kernel wait expired            */
 #define GQA_ERR_WORKSPACE 6     /* workspace missing or too small              */
 #define GQA_ERR_NO_DEVICE 7     /* no sm_100 device current                    */
+#define GQA_ERR_SCRATCH_LIMIT 8 /* problem needs more than the static scratch  */
 
 #define GQA_DTYPE_F16 0
 #define GQA_DTYPE_BF16 1
@@ -105,6 +106,28 @@ int gqa_split_fused(const void* q, const void* k, const void* v, void* o, const 
                     int batch, int num_heads, int num_kv_heads, int seq_q, int seq_kv, int head_dim,
                     float scale_log2, int causal, int dtype, void* workspace, size_t workspace_bytes,
                     void* stream);
+
+/*
+ * gqa_split_fused without a workspace argument, for callers that cannot
+ * allocate device memory -- e.g. a host bound to this C ABI through an FFI
+ * (Go, Java, Rust) that owns no CUDA allocator, or an engine that reserves all
+ * of HBM for its own pool up front, where a cudaMalloc would fail or stall the
+ * device in the middle of a decode step. The scratch lives in a static
+ * __device__ array of GQA_NOALLOC_SCRATCH_BYTES that every GPU loading the
+ * library holds until the process exits; the library calls no cudaMalloc,
+ * cudaFree or allocating routine here. Problems whose scratch would exceed it
+ * return GQA_ERR_SCRATCH_LIMIT (gqa_split_fused_workspace_bytes gives the
+ * need). The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call
+ * before any stream capture. All calls share the one array: calls that
+ * overlap on the GPU (other streams, other threads) race and must be ordered
+ * by the caller. No counterpart in the reference.
+ */
+#define GQA_NOALLOC_SCRATCH_BYTES (4u << 20)
+int gqa_split_fused_noalloc(const void* q, const void* k, const void* v, void* o, const int64_t* q_strides4,
+                            const int64_t* k_strides4, const int64_t* v_strides4, const int64_t* o_strides4,
+                            int batch, int num_heads, int num_kv_heads, int seq_q, int seq_kv, int head_dim,
+                            float scale_log2, int causal, int dtype, void* stream);
 
 /*
  * Partial attention over one shard of the key axis, for a key range split
