@@ -394,6 +394,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode half of the default line")
+    ap.add_argument("--decode-steps", type=int, default=5000, help="timed steps of the decode half")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -462,12 +463,12 @@ def main():
     if args.workload == "prefill" and not args.no_decode:
         dwl = WORKLOADS["decode"]
         dargs = argparse.Namespace(**{**vars(args), "workload": "decode"})
-        dres = run_attention_workload(dwl, world, rank, device, 5000, args.warmup, dargs)
+        dres = run_attention_workload(dwl, world, rank, device, args.decode_steps, args.warmup, dargs)
         dl_ms = dres["mean_ms_rank0"]
         dbytes = attn_bytes(1, 32, 8, 1, 16384, 128)
         line["decode_16k"] = {"value": round(dres["value"], 1), "unit": "GB/s",
                               "us_per_step": round(dres["ms_per_step"] * 1e3, 2),
-                              "steps": 5000, "scaling": "weak",
+                              "steps": args.decode_steps, "scaling": "weak",
                               "roofline": {"bound": "hbm", "achieved": round(dbytes / (dl_ms * 1e-3) / 1e9, 1),
                                            "peak": peaks["hbm"], "unit": "GB/s",
                                            "frac": round(dbytes / (dl_ms * 1e-3) / 1e9 / peaks["hbm"], 4),

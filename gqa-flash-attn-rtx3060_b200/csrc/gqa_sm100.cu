@@ -154,7 +154,7 @@ int launch_status() {
 // ----------------------------------------------------------------------------- streaming plan
 // Number of packed rows (group * block_m) the streaming kernel handles per unit.
 constexpr int kStreamMaxRows = 64;
-constexpr int kStreamCtasPerSm = 2;
+constexpr int kStreamCtasPerSm = 1;
 constexpr int kMaxSplits = 64;
 
 struct StreamPlan {
@@ -172,19 +172,22 @@ StreamPlan plan_stream(const Shape& s, int sm_count, bool allow_split) {
   pl.nsplit = 1;
   pl.chunk = stages * 64;
   if (!allow_split) return pl;
+  // Cost of a plan in units of one 64-key stage of streaming: every wave of CTAs
+  // takes its chunk's stages plus a fixed per-CTA cost (set-up, pipeline ramp,
+  // publishing the partial), about kFixedStages. Fewer waves beat a finer
+  // balance: a second wave restarts the ramp.
+  constexpr double kFixedStages = 5.0;
   const double slots = (double)sm_count * kStreamCtasPerSm;
-  double best = -1.0;
+  double best = 1e300;
   const int max_ns = std::min(std::min(stages, kMaxSplits), std::max(1, 4096 / pl.rows));
   for (int ns = 1; ns <= max_ns; ++ns) {
     const int chunk_st = (stages + ns - 1) / ns;
     const int ns_eff = (stages + chunk_st - 1) / chunk_st;
     if (ns_eff != ns) continue;
-    const double ctas = (double)pl.units * ns_eff;
-    const double waves = std::ceil(ctas / slots);
-    // fraction of SM-time doing useful streaming, all CTAs of a wave costing chunk_st stages
-    const double eff = ((double)pl.units * stages) / (waves * slots * chunk_st);
-    if (eff > best + 1e-3) {
-      best = eff;
+    const double waves = std::ceil((double)pl.units * ns_eff / slots);
+    const double cost = waves * (chunk_st + kFixedStages);
+    if (cost < best - 1e-9) {
+      best = cost;
       pl.nsplit = ns;
       pl.chunk = chunk_st * 64;
     }
@@ -219,9 +222,9 @@ cudaError_t launch_stream_hd(const StreamParams& p, const StreamPlan& pl, const 
   const dim3 grid(pl.units * pl.nsplit);
   const int smem = StreamCfg<HD>::kSmemBytes;
   switch (pl.rg) {
-    case 1: gqa_stream_kernel<HD, BF, 1><<<grid, 160, smem, st>>>(p, km, vm); break;
-    case 2: gqa_stream_kernel<HD, BF, 2><<<grid, 160, smem, st>>>(p, km, vm); break;
-    default: gqa_stream_kernel<HD, BF, 4><<<grid, 160, smem, st>>>(p, km, vm); break;
+    case 1: gqa_stream_kernel<HD, BF, 1><<<grid, StreamCfg<HD>::kThreads, smem, st>>>(p, km, vm); break;
+    case 2: gqa_stream_kernel<HD, BF, 2><<<grid, StreamCfg<HD>::kThreads, smem, st>>>(p, km, vm); break;
+    default: gqa_stream_kernel<HD, BF, 4><<<grid, StreamCfg<HD>::kThreads, smem, st>>>(p, km, vm); break;
   }
   return cudaGetLastError();
 }

@@ -3,7 +3,10 @@
 // (batch, kv_head, q-block) unit through a TMA ring and keeps the online
 // softmax state of up to 64 packed rows (group_size heads x block_m positions)
 // in mma.sync accumulators. At <= 64 rows per 512 bytes of K+V the kernel is
-// bound by HBM bandwidth, not by the tensor pipe.
+// bound by HBM bandwidth, not by the tensor pipe; what matters is keeping
+// enough bytes in flight (a 192 KB ring, one CTA per SM) and enough warps
+// (eight compute warps, two per SM sub-partition) to hide the MMA/shuffle
+// latency of each stage behind the next stage's arrival.
 //
 // Reference behaviour followed:
 //   gqa_kernels/gqa_split.py:46-112   per-chunk partial (m, l, acc), causal chunk clip
@@ -32,7 +35,7 @@ struct StreamParams {
   int n_mtiles;   // ceil(seq_q / block_m)
   int rows;       // group * block_m packed rows per unit (<= 16 * RG)
   int nsplit;     // chunks per unit (gridDim.x = units * nsplit)
-  int chunk;      // keys per chunk
+  int chunk;      // keys per chunk (a multiple of 64, or the reference's chunk size)
   int causal;
   float scale_log2;
   int kv_offset;     // global position of local key 0
@@ -57,28 +60,37 @@ struct StreamParams {
 
 template <int HD>
 struct StreamCfg {
-  static constexpr int kBN = 64;                       // keys per stage
+  static constexpr int kBN = 128;                      // keys per stage
+  static constexpr int kBox = 64;                      // keys per TMA box
   static constexpr int kNSub = HD / 64;                // 128-byte swizzle sub-tiles along d
-  static constexpr int kSubBytes = kBN * 128;          // one sub-tile: 64 keys x 128 B
+  static constexpr int kSubBytes = kBN * 128;          // one d sub-tile over the stage's keys
+  static constexpr int kBoxBytes = kBox * 128;         // one TMA box
   static constexpr int kTileBytes = kNSub * kSubBytes;  // K (or V) stage
   static constexpr int kStageBytes = 2 * kTileBytes;
   static constexpr int kStages = (HD == 128) ? 3 : 6;
-  static constexpr int kRingBytes = kStages * kStageBytes;  // 96 KB
-  // barriers + flags after the ring
-  static constexpr int kSmemBytes = kRingBytes + 2 * kStages * 8 + 64 + 1024;
-  static constexpr int kThreads = 160;  // 4 compute warps + 1 TMA producer warp
+  static constexpr int kRingBytes = kStages * kStageBytes;  // 192 KB: one CTA per SM
+  static constexpr int kWarps = 8;                          // compute warps
+  static constexpr int kThreads = (kWarps + 1) * 32;        // + one TMA producer warp
+  // barriers (full[kStages], empty[kStages], combine) + flags after the ring
+  static constexpr int kBarBytes = (2 * kStages + 1) * 8;
+  static constexpr int kSmemBytes = kRingBytes + kBarBytes + 64 + 1024;
 };
 
+#define GQA_CBAR() asm volatile("bar.sync 1, 256;" ::: "memory")  // the 8 compute warps
+
 template <int HD, bool BF16, int RG>
-__global__ void __launch_bounds__(160, 2)
+__global__ void __launch_bounds__(288, 1)
     gqa_stream_kernel(const StreamParams p, const __grid_constant__ CUtensorMap kmap,
                       const __grid_constant__ CUtensorMap vmap) {
   using Cfg = StreamCfg<HD>;
-  constexpr int KS = 4 / RG;        // warps sharing one row group split the stage's keys
-  constexpr int NKW = Cfg::kBN / KS;  // keys per warp per stage (16, 32, 64)
-  constexpr int NNB = NKW / 8;       // n8 blocks per warp per stage
-  constexpr int NDB = HD / 8;        // n8 blocks along d
-  constexpr int NKS = HD / 16;       // k16 steps along d
+  constexpr int NW = Cfg::kWarps;
+  constexpr int KS = NW / RG;           // warps sharing one row group split the stage's keys
+  constexpr int NKW = Cfg::kBN / KS;    // keys per warp per stage (16, 32, 64)
+  constexpr int NNB = NKW / 8;          // n8 blocks per warp per stage
+  constexpr int NDB = HD / 8;           // n8 blocks along d
+  constexpr int NKS = HD / 16;          // k16 steps along d
+  constexpr int CT = NW * 32;           // compute threads
+  static_assert(NKW >= 16, "a warp needs at least one k16 block of keys");
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_base = smem_u32(smem_raw);
@@ -86,8 +98,9 @@ __global__ void __launch_bounds__(160, 2)
   uint8_t* const smem = smem_raw + (base - raw_base);
   const uint32_t bar_full = base + Cfg::kRingBytes;
   const uint32_t bar_empty = bar_full + Cfg::kStages * 8;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kRingBytes + 2 * Cfg::kStages * 8);
-  int* last_flag = reinterpret_cast<int*>(smem + Cfg::kRingBytes + 2 * Cfg::kStages * 8 + 4);
+  const uint32_t bar_comb = bar_empty + Cfg::kStages * 8;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kRingBytes + Cfg::kBarBytes);
+  int* last_flag = reinterpret_cast<int*>(smem + Cfg::kRingBytes + Cfg::kBarBytes + 4);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -111,101 +124,113 @@ __global__ void __launch_bounds__(160, 2)
   const int k_end = min(k_begin + p.chunk, kv_end);
   const int n_stages = (k_end > k_begin) ? (k_end - k_begin + Cfg::kBN - 1) / Cfg::kBN : 0;
 
-  if (tid == 0) {
+  // The producer thread initialises the barriers and issues the first ring of
+  // loads before the CTA-wide barrier, so HBM requests start at once. A stage
+  // holds one or two 64-key boxes of K and of V (the chunk's last stage may be half).
+  auto issue = [&](int t) {
+    const int slot = t % Cfg::kStages;
+    const uint32_t full = bar_full + 8 * slot;
+    const int key0 = k_begin + t * Cfg::kBN;
+    const int halves = (min(Cfg::kBN, k_end - key0) + Cfg::kBox - 1) / Cfg::kBox;
+    mbar_arrive_expect_tx(full, halves * 2 * Cfg::kNSub * Cfg::kBoxBytes);
+    const uint32_t kdst = base + slot * Cfg::kStageBytes;
+    const uint32_t vdst = kdst + Cfg::kTileBytes;
+    for (int h = 0; h < halves; ++h) {
+#pragma unroll
+      for (int s = 0; s < Cfg::kNSub; ++s) {
+        const uint32_t o = s * Cfg::kSubBytes + h * Cfg::kBoxBytes;
+        tma_load_4d(kdst + o, &kmap, full, s * 64, key0 + h * Cfg::kBox, kvh, b);
+        tma_load_4d(vdst + o, &vmap, full, s * 64, key0 + h * Cfg::kBox, kvh, b);
+      }
+    }
+  };
+  const int n_first = min(n_stages, Cfg::kStages);
+  if (tid == CT) {
     for (int s = 0; s < Cfg::kStages; ++s) {
       mbar_init(bar_full + 8 * s, 1);
-      mbar_init(bar_empty + 8 * s, 4);
+      mbar_init(bar_empty + 8 * s, NW);
     }
+    mbar_init(bar_comb, 1);
     *abort_flag = 0;
     fence_mbar_init();
     fence_proxy_async_smem();
+    if (n_stages > 0) {
+      tma_prefetch_desc(&kmap);
+      tma_prefetch_desc(&vmap);
+    }
+    for (int t = 0; t < n_first; ++t) issue(t);
   }
   __syncthreads();
 
-  if (warp == 4) {
+  if (warp == NW) {
     // ---------------------------------------------------------------- producer
     if (lane == 0 && n_stages > 0) {
-      tma_prefetch_desc(&kmap);
-      tma_prefetch_desc(&vmap);
-      int t = 0;
+      int t = n_first;
       for (; t < n_stages; ++t) {
         const int slot = t % Cfg::kStages;
-        const int use = t / Cfg::kStages;
-        if (use > 0 && !mbar_wait(bar_empty + 8 * slot, (use - 1) & 1, abort_flag, 101)) break;
-        const uint32_t full = bar_full + 8 * slot;
-        mbar_arrive_expect_tx(full, Cfg::kStageBytes);
-        const int key0 = k_begin + t * Cfg::kBN;
-        const uint32_t kdst = base + slot * Cfg::kStageBytes;
-        const uint32_t vdst = kdst + Cfg::kTileBytes;
-#pragma unroll
-        for (int s = 0; s < Cfg::kNSub; ++s) {
-          tma_load_4d(kdst + s * Cfg::kSubBytes, &kmap, full, s * 64, key0, kvh, b);
-          tma_load_4d(vdst + s * Cfg::kSubBytes, &vmap, full, s * 64, key0, kvh, b);
-        }
+        if (!mbar_wait(bar_empty + 8 * slot, (t / Cfg::kStages - 1) & 1, abort_flag, 101)) break;
+        issue(t);
       }
       // On abort, let the loads already issued land before the CTA exits.
       if (t < n_stages) {
         for (int u = max(0, t - Cfg::kStages); u < t; ++u) {
-          const int slot = u % Cfg::kStages;
           volatile int dummy = 0;
-          mbar_wait(bar_full + 8 * slot, (u / Cfg::kStages) & 1, &dummy, 102);
+          mbar_wait(bar_full + 8 * (u % Cfg::kStages), (u / Cfg::kStages) & 1, &dummy, 102);
         }
       }
     }
-  } else {
-    // ----------------------------------------------------------------- compute
-    const int rg = warp % RG;
-    const int ks = warp / RG;
-    const int gr = lane >> 2;
-    const int gc = lane & 3;
+    return;
+  }
 
-    // Packed rows owned by this thread: r0 = rg*16 + gr, r1 = r0 + 8.
-    int row_r[2];
-    bool valid_r[2];
-    int lim_r[2];  // local key limit (exclusive) for each row, clipped to the chunk
-    const uint16_t* qrow[2];
+  // ------------------------------------------------------------------- compute
+  const int rg = warp % RG;
+  const int ks = warp / RG;
+  const int gr = lane >> 2;
+  const int gc = lane & 3;
+
+  // Packed rows owned by this thread: r0 = rg*16 + gr, r1 = r0 + 8.
+  int lim_r[2];  // local key limit (exclusive) for each row, clipped to the chunk
+  const uint16_t* qrow[2];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int r = rg * 16 + gr + 8 * h;
-      row_r[h] = r;
-      const int g = r / p.block_m;
-      const int m = r - g * p.block_m;
-      const int pos = mt * p.block_m + m;
-      valid_r[h] = (r < p.rows) && (pos < p.seq_q);
-      int lim = k_end;
-      if (p.causal) lim = min(lim, pos + off - p.kv_offset + 1);
-      lim_r[h] = lim;
-      qrow[h] = valid_r[h] ? p.q + b * p.q_sb + (int64_t)(kvh * p.group + g) * p.q_sh + (int64_t)pos * p.q_sm
-                           : nullptr;
-    }
+  for (int h = 0; h < 2; ++h) {
+    const int r = rg * 16 + gr + 8 * h;
+    const int g = r / p.block_m;
+    const int m = r - g * p.block_m;
+    const int pos = mt * p.block_m + m;
+    const bool valid = (r < p.rows) && (pos < p.seq_q);
+    int lim = k_end;
+    if (p.causal) lim = min(lim, pos + off - p.kv_offset + 1);
+    lim_r[h] = lim;
+    qrow[h] = valid ? p.q + b * p.q_sb + (int64_t)(kvh * p.group + g) * p.q_sh + (int64_t)pos * p.q_sm : nullptr;
+  }
 
-    // Q fragments (A operand, 16 rows x HD), loaded once.
-    uint32_t qa[NKS][4];
+  // Q fragments (A operand, 16 rows x HD), loaded once.
+  uint32_t qa[NKS][4];
 #pragma unroll
-    for (int kk = 0; kk < NKS; ++kk) {
-      const int d0 = kk * 16 + gc * 2;
-      qa[kk][0] = qrow[0] ? *reinterpret_cast<const uint32_t*>(qrow[0] + d0) : 0u;
-      qa[kk][1] = qrow[1] ? *reinterpret_cast<const uint32_t*>(qrow[1] + d0) : 0u;
-      qa[kk][2] = qrow[0] ? *reinterpret_cast<const uint32_t*>(qrow[0] + d0 + 8) : 0u;
-      qa[kk][3] = qrow[1] ? *reinterpret_cast<const uint32_t*>(qrow[1] + d0 + 8) : 0u;
-    }
+  for (int kk = 0; kk < NKS; ++kk) {
+    const int d0 = kk * 16 + gc * 2;
+    qa[kk][0] = qrow[0] ? *reinterpret_cast<const uint32_t*>(qrow[0] + d0) : 0u;
+    qa[kk][1] = qrow[1] ? *reinterpret_cast<const uint32_t*>(qrow[1] + d0) : 0u;
+    qa[kk][2] = qrow[0] ? *reinterpret_cast<const uint32_t*>(qrow[0] + d0 + 8) : 0u;
+    qa[kk][3] = qrow[1] ? *reinterpret_cast<const uint32_t*>(qrow[1] + d0 + 8) : 0u;
+  }
 
-    float acc[NDB][4];
+  float acc[NDB][4];
 #pragma unroll
-    for (int i = 0; i < NDB; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-    float m_run[2] = {-INFINITY, -INFINITY};
-    float l_run[2] = {0.f, 0.f};
-    const float scale = p.scale_log2;
+  for (int i = 0; i < NDB; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY};
+  float l_run[2] = {0.f, 0.f};
+  const float scale = p.scale_log2;
 
-    for (int t = 0; t < n_stages; ++t) {
-      const int slot = t % Cfg::kStages;
-      bool ok = mbar_wait(bar_full + 8 * slot, (t / Cfg::kStages) & 1, abort_flag, 103);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
-      const uint32_t kst = base + slot * Cfg::kStageBytes;
-      const uint32_t vst = kst + Cfg::kTileBytes;
-      const int key_w = k_begin + t * Cfg::kBN + ks * NKW;  // first key of this warp's block
-
+  for (int t = 0; t < n_stages; ++t) {
+    const int slot = t % Cfg::kStages;
+    bool ok = mbar_wait(bar_full + 8 * slot, (t / Cfg::kStages) & 1, abort_flag, 103);
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok) break;
+    const uint32_t kst = base + slot * Cfg::kStageBytes;
+    const uint32_t vst = kst + Cfg::kTileBytes;
+    const int key_w = k_begin + t * Cfg::kBN + ks * NKW;  // first key of this warp's block
+    if (key_w < k_end) {  // warp-uniform: blocks past the chunk end were not loaded
       // ---- S = Q K^T over this warp's NKW keys
       float s[NNB][4];
 #pragma unroll
@@ -286,189 +311,241 @@ __global__ void __launch_bounds__(160, 2)
           mma_16816<BF16>(acc[dc + 1], pa, b2, b3);
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar_empty + 8 * slot);
     }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar_empty + 8 * slot);
+  }
 
-    // Row sums are per-thread partials over the quad's columns.
+  // Row sums are per-thread partials over the quad's columns.
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 1);
-      l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 2);
+  for (int h = 0; h < 2; ++h) {
+    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 1);
+    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 2);
+  }
+
+  // ---- merge the KS warps of each row group through shared memory
+  GQA_CBAR();  // every compute warp is done with the ring
+  float* mbuf = reinterpret_cast<float*>(smem);  // [NW][16]
+  float* lbuf = mbuf + NW * 16;                  // [NW][16]
+  float* abuf = lbuf + NW * 16;                  // [NW][16][HD]
+  {
+    float* aw = abuf + warp * 16 * HD;
+#pragma unroll
+    for (int i = 0; i < NDB; ++i) {
+      const int d = i * 8 + gc * 2;
+      *reinterpret_cast<float2*>(aw + gr * HD + d) = make_float2(acc[i][0], acc[i][1]);
+      *reinterpret_cast<float2*>(aw + (gr + 8) * HD + d) = make_float2(acc[i][2], acc[i][3]);
     }
+    if (gc == 0) {
+      mbuf[warp * 16 + gr] = m_run[0];
+      mbuf[warp * 16 + gr + 8] = m_run[1];
+      lbuf[warp * 16 + gr] = l_run[0];
+      lbuf[warp * 16 + gr + 8] = l_run[1];
+    }
+  }
+  GQA_CBAR();
 
-    // ---- merge the KS warps of each row group through shared memory
-    asm volatile("bar.sync 1, 128;" ::: "memory");  // every warp is done with the ring
-    float* mbuf = reinterpret_cast<float*>(smem);               // [4][16]
-    float* lbuf = mbuf + 64;                                    // [4][16]
-    float* abuf = lbuf + 64;                                    // [4][16][HD]
-    {
-      float* aw = abuf + warp * 16 * HD;
+  // Combined per-row (M, L) of this CTA and the per-warp weights.
+  float* fin_m = abuf + NW * 16 * HD;  // [64]
+  float* fin_l = fin_m + 64;           // [64]
+  float* fin_w = fin_l + 64;           // [64][KS]
+  if (tid < RG * 16) {
+    const int r = tid;
+    const int g_rg = r / 16, rr = r % 16;
+    float M = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < NDB; ++i) {
-        const int d = i * 8 + gc * 2;
-        *reinterpret_cast<float2*>(aw + gr * HD + d) = make_float2(acc[i][0], acc[i][1]);
-        *reinterpret_cast<float2*>(aw + (gr + 8) * HD + d) = make_float2(acc[i][2], acc[i][3]);
-      }
-      if (gc == 0) {
-        mbuf[warp * 16 + gr] = m_run[0];
-        mbuf[warp * 16 + gr + 8] = m_run[1];
-        lbuf[warp * 16 + gr] = l_run[0];
-        lbuf[warp * 16 + gr + 8] = l_run[1];
+    for (int k2 = 0; k2 < KS; ++k2) M = fmaxf(M, mbuf[(k2 * RG + g_rg) * 16 + rr]);
+    const float Mu = (M == -INFINITY) ? 0.f : M;
+    float L = 0.f;
+#pragma unroll
+    for (int k2 = 0; k2 < KS; ++k2) {
+      const int w = k2 * RG + g_rg;
+      const float wt = fast_exp2(mbuf[w * 16 + rr] - Mu);
+      fin_w[r * KS + k2] = wt;
+      L += wt * lbuf[w * 16 + rr];
+    }
+    fin_m[r] = M;
+    fin_l[r] = L;
+  }
+  GQA_CBAR();
+
+  // This CTA's combined acc for packed row r, columns d..d+3.
+  auto cta_acc = [&](int r, int d) {
+    const int g_rg = r / 16, rr = r % 16;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int k2 = 0; k2 < KS; ++k2) {
+      const float wt = fin_w[r * KS + k2];
+      const float4 v = *reinterpret_cast<const float4*>(abuf + ((k2 * RG + g_rg) * 16 + rr) * HD + d);
+      a.x += wt * v.x;
+      a.y += wt * v.y;
+      a.z += wt * v.z;
+      a.w += wt * v.w;
+    }
+    return a;
+  };
+
+  const int n_rows = min(p.rows, RG * 16);
+  constexpr int per_row = HD / 4;
+  if (p.mode == kStreamOut) {
+    for (int idx = tid; idx < n_rows * per_row; idx += CT) {
+      const int r = idx / per_row, d = (idx - r * per_row) * 4;
+      const int g = r / p.block_m, m = r - g * p.block_m, pos = mt * p.block_m + m;
+      if (pos >= p.seq_q) continue;
+      const float4 a = cta_acc(r, d);
+      const float inv = 1.f / fin_l[r];  // l == 0 (no visible key) -> NaN, as the reference
+      uint2 pk;
+      pk.x = pack2<BF16>(a.x * inv, a.y * inv);
+      pk.y = pack2<BF16>(a.z * inv, a.w * inv);
+      uint16_t* dst = reinterpret_cast<uint16_t*>(p.o) + b * p.o_sb + (int64_t)(kvh * p.group + g) * p.o_sh +
+                      (int64_t)pos * p.o_sm + d;
+      *reinterpret_cast<uint2*>(dst) = pk;
+    }
+    return;
+  }
+  if (p.mode == kStreamRefPartial) {
+    for (int idx = tid; idx < n_rows * per_row; idx += CT) {
+      const int r = idx / per_row, d = (idx - r * per_row) * 4;
+      const int g = r / p.block_m, m = r - g * p.block_m, pos = mt * p.block_m + m;
+      if (pos >= p.seq_q) continue;
+      const int head = kvh * p.group + g;
+      const float4 a = cta_acc(r, d);
+      float* ap = p.acc_p + b * p.a_sb + head * p.a_sh + (int64_t)pos * p.a_sm + (int64_t)split * p.a_ss;
+      ap[(int64_t)(d + 0) * p.a_sd] = a.x;
+      ap[(int64_t)(d + 1) * p.a_sd] = a.y;
+      ap[(int64_t)(d + 2) * p.a_sd] = a.z;
+      ap[(int64_t)(d + 3) * p.a_sd] = a.w;
+      if (d == 0) {
+        const int64_t po = b * p.p_sb + head * p.p_sh + (int64_t)pos * p.p_sm + (int64_t)split * p.p_ss;
+        p.m_p[po] = fin_m[r];
+        p.l_p[po] = fin_l[r];
       }
     }
-    asm volatile("bar.sync 1, 128;" ::: "memory");
+    return;
+  }
 
-    // Combined per-row (M, L) for the rows of this CTA -> fin buffers.
-    float* fin_m = abuf + 4 * 16 * HD;  // [64]
-    float* fin_l = fin_m + 64;          // [64]
-    float* fin_w = fin_l + 64;          // [64][4] per-warp weights
-    if (tid < RG * 16) {
-      const int r = tid;
-      const int g_rg = r / 16, rr = r % 16;
-      float M = -INFINITY;
-#pragma unroll
-      for (int k2 = 0; k2 < KS; ++k2) M = fmaxf(M, mbuf[(k2 * RG + g_rg) * 16 + rr]);
-      const float Mu = (M == -INFINITY) ? 0.f : M;
-      float L = 0.f;
-#pragma unroll
-      for (int k2 = 0; k2 < KS; ++k2) {
-        const int w = k2 * RG + g_rg;
-        const float wt = fast_exp2(mbuf[w * 16 + rr] - Mu);
-        fin_w[r * 4 + k2] = wt;
-        L += wt * lbuf[w * 16 + rr];
-      }
-      fin_m[r] = M;
-      fin_l[r] = L;
+  // ---- kStreamFused / kStreamFusedPartial: publish this chunk's partial.
+  const int64_t wbase = ((int64_t)unit * p.nsplit + split) * p.rows;
+  for (int idx = tid; idx < n_rows * per_row; idx += CT) {
+    const int r = idx / per_row, d = (idx - r * per_row) * 4;
+    __stcg(reinterpret_cast<float4*>(p.ws_acc + (wbase + r) * HD + d), cta_acc(r, d));
+    if (d == 0) {
+      __stcg(p.ws_m + wbase + r, fin_m[r]);
+      __stcg(p.ws_l + wbase + r, fin_l[r]);
     }
-    asm volatile("bar.sync 1, 128;" ::: "memory");
+  }
+  // The CTA barrier orders every thread's partial stores before thread 0's
+  // release-acquire ticket (fences are cumulative); the last CTA acquires them.
+  GQA_CBAR();
+  if (tid == 0) {
+    unsigned ticket;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(ticket) : "l"(p.ws_cnt + unit) : "memory");
+    *last_flag = (ticket == (unsigned)(p.nsplit - 1)) ? 1 : 0;
+  }
+  GQA_CBAR();
+  if (!*last_flag) return;
 
-    // Cooperative pass over (row, 4 consecutive d): combined acc -> destination.
-    const int n_rows = min(p.rows, RG * 16);
-    const int per_row = HD / 4;
-    if (p.mode == kStreamOut) {
-      for (int idx = tid; idx < n_rows * per_row; idx += 128) {
-        const int r = idx / per_row, d = (idx - r * per_row) * 4;
-        const int g = r / p.block_m, m = r - g * p.block_m, pos = mt * p.block_m + m;
-        if (pos >= p.seq_q) continue;
-        const int g_rg = r / 16, rr = r % 16;
-        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+  // ---- last CTA of the unit: log-sum-exp combine of all chunk partials.
+  // Shared-memory layout (the ring is free now):
+  //   sm_m, sm_l, sm_w [nsplit][rows]  partial m, l and combine weights
+  //   fm, fl [64]                      combined M and L per row
+  //   cacc [nsplit][rows][HD]          the unit's acc partials, staged by one bulk copy when they fit
+  const int64_t ubase = (int64_t)unit * p.nsplit * p.rows;
+  const int nsr = p.nsplit * n_rows;
+  float* sm_m = reinterpret_cast<float*>(smem);
+  float* sm_l = sm_m + nsr;
+  float* sm_w = sm_l + nsr;
+  float* fm = sm_w + nsr;
+  float* fl = fm + 64;
+  const uint32_t small_bytes = ((uint32_t)(3 * nsr + 128) * 4u + 15u) & ~15u;
+  const uint32_t acc_bytes = (uint32_t)nsr * HD * 4u;
+  const bool staged = small_bytes + acc_bytes <= (uint32_t)Cfg::kRingBytes;
+  float* cacc = reinterpret_cast<float*>(smem + small_bytes);
+  if (staged && tid == 0) {
+    // Other CTAs wrote the partials with generic stores; this read goes through the async proxy.
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    mbar_arrive_expect_tx(bar_comb, acc_bytes);
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(cacc)),
+                 "l"(reinterpret_cast<uint64_t>(p.ws_acc + ubase * HD)), "r"(acc_bytes), "r"(bar_comb)
+                 : "memory");
+  }
+  for (int i = tid; i < nsr; i += CT) {
+    sm_m[i] = __ldcg(p.ws_m + ubase + i);
+    sm_l[i] = __ldcg(p.ws_l + ubase + i);
+  }
+  GQA_CBAR();
+  // Per-row weights over the unit's chunks, w_s = exp2(m_s - max_s m_s): one warp per
+  // row, lanes over chunks, shuffle reductions.
+  for (int r = warp; r < n_rows; r += NW) {
+    float M = -INFINITY;
+    for (int s2 = lane; s2 < p.nsplit; s2 += 32) M = fmaxf(M, sm_m[s2 * n_rows + r]);
 #pragma unroll
-        for (int k2 = 0; k2 < KS; ++k2) {
-          const float wt = fin_w[r * 4 + k2];
-          const float4 v = *reinterpret_cast<const float4*>(abuf + ((k2 * RG + g_rg) * 16 + rr) * HD + d);
-          a.x += wt * v.x; a.y += wt * v.y; a.z += wt * v.z; a.w += wt * v.w;
-        }
-        const float inv = 1.f / fin_l[r];  // l == 0 (no visible key) -> NaN, as the reference
-        uint2 pk;
-        pk.x = pack2<BF16>(a.x * inv, a.y * inv);
-        pk.y = pack2<BF16>(a.z * inv, a.w * inv);
-        uint16_t* dst = reinterpret_cast<uint16_t*>(p.o) + b * p.o_sb + (int64_t)(kvh * p.group + g) * p.o_sh +
-                        (int64_t)pos * p.o_sm + d;
-        *reinterpret_cast<uint2*>(dst) = pk;
-      }
-    } else if (p.mode == kStreamRefPartial) {
-      for (int idx = tid; idx < n_rows * per_row; idx += 128) {
-        const int r = idx / per_row, d = (idx - r * per_row) * 4;
-        const int g = r / p.block_m, m = r - g * p.block_m, pos = mt * p.block_m + m;
-        if (pos >= p.seq_q) continue;
-        const int g_rg = r / 16, rr = r % 16;
-        const int head = kvh * p.group + g;
-        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    const float Mu = (M == -INFINITY) ? 0.f : M;
+    float L = 0.f;
+    for (int s2 = lane; s2 < p.nsplit; s2 += 32) {
+      const float wt = fast_exp2(sm_m[s2 * n_rows + r] - Mu);
+      sm_w[s2 * n_rows + r] = wt;
+      L += wt * sm_l[s2 * n_rows + r];
+    }
 #pragma unroll
-        for (int k2 = 0; k2 < KS; ++k2) {
-          const float wt = fin_w[r * 4 + k2];
-          const float4 v = *reinterpret_cast<const float4*>(abuf + ((k2 * RG + g_rg) * 16 + rr) * HD + d);
-          a.x += wt * v.x; a.y += wt * v.y; a.z += wt * v.z; a.w += wt * v.w;
-        }
-        float* ap = p.acc_p + b * p.a_sb + head * p.a_sh + (int64_t)pos * p.a_sm + (int64_t)split * p.a_ss;
-        ap[(int64_t)(d + 0) * p.a_sd] = a.x;
-        ap[(int64_t)(d + 1) * p.a_sd] = a.y;
-        ap[(int64_t)(d + 2) * p.a_sd] = a.z;
-        ap[(int64_t)(d + 3) * p.a_sd] = a.w;
-        if (d == 0) {
-          const int64_t po = b * p.p_sb + head * p.p_sh + (int64_t)pos * p.p_sm + (int64_t)split * p.p_ss;
-          p.m_p[po] = fin_m[r];
-          p.l_p[po] = fin_l[r];
-        }
+    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    if (lane == 0) {
+      fm[r] = M;
+      fl[r] = L;
+    }
+  }
+  GQA_CBAR();
+  if (staged) mbar_wait(bar_comb, 0, abort_flag, 104);
+  for (int idx = tid; idx < n_rows * per_row; idx += CT) {
+    const int r = idx / per_row, d = (idx - r * per_row) * 4;
+    const int g = r / p.block_m, m = r - g * p.block_m, pos = mt * p.block_m + m;
+    if (pos >= p.seq_q) continue;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (staged) {
+#pragma unroll 4
+      for (int s2 = 0; s2 < p.nsplit; ++s2) {
+        const float wt = sm_w[s2 * n_rows + r];
+        const float4 v = *reinterpret_cast<const float4*>(cacc + (s2 * n_rows + r) * HD + d);
+        a.x += wt * v.x;
+        a.y += wt * v.y;
+        a.z += wt * v.z;
+        a.w += wt * v.w;
       }
     } else {
-      // kStreamFused / kStreamFusedPartial: publish this chunk's partial.
-      const int64_t wbase = ((int64_t)unit * p.nsplit + split) * p.rows;
-      for (int idx = tid; idx < n_rows * per_row; idx += 128) {
-        const int r = idx / per_row, d = (idx - r * per_row) * 4;
-        const int g_rg = r / 16, rr = r % 16;
-        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int k2 = 0; k2 < KS; ++k2) {
-          const float wt = fin_w[r * 4 + k2];
-          const float4 v = *reinterpret_cast<const float4*>(abuf + ((k2 * RG + g_rg) * 16 + rr) * HD + d);
-          a.x += wt * v.x; a.y += wt * v.y; a.z += wt * v.z; a.w += wt * v.w;
-        }
-        __stcg(reinterpret_cast<float4*>(p.ws_acc + (wbase + r) * HD + d), a);
-        if (d == 0) {
-          __stcg(p.ws_m + wbase + r, fin_m[r]);
-          __stcg(p.ws_l + wbase + r, fin_l[r]);
-        }
+#pragma unroll 8
+      for (int s2 = 0; s2 < p.nsplit; ++s2) {
+        const float wt = sm_w[s2 * n_rows + r];
+        const float4 v =
+            __ldcg(reinterpret_cast<const float4*>(p.ws_acc + (ubase + (int64_t)s2 * p.rows + r) * HD + d));
+        a.x += wt * v.x;
+        a.y += wt * v.y;
+        a.z += wt * v.z;
+        a.w += wt * v.w;
       }
-      __threadfence();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (tid == 0) {
-        const unsigned ticket = atomicAdd(p.ws_cnt + unit, 1u);
-        *last_flag = (ticket == (unsigned)(p.nsplit - 1)) ? 1 : 0;
-      }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (*last_flag) {
-        __threadfence();
-        // Per-row weights over the unit's chunks: w_s = exp2(m_s - max_s m_s).
-        float* wsm = fin_w + 64 * 4;  // [rows][nsplit], rows * nsplit <= 4096 (host-enforced)
-        const int64_t ubase = (int64_t)unit * p.nsplit * p.rows;
-        for (int r = tid; r < n_rows; r += 128) {
-          float M = -INFINITY;
-          for (int s2 = 0; s2 < p.nsplit; ++s2) M = fmaxf(M, __ldcg(p.ws_m + ubase + (int64_t)s2 * p.rows + r));
-          const float Mu = (M == -INFINITY) ? 0.f : M;
-          float L = 0.f;
-          for (int s2 = 0; s2 < p.nsplit; ++s2) {
-            const float wt = fast_exp2(__ldcg(p.ws_m + ubase + (int64_t)s2 * p.rows + r) - Mu);
-            wsm[r * p.nsplit + s2] = wt;
-            L += wt * __ldcg(p.ws_l + ubase + (int64_t)s2 * p.rows + r);
-          }
-          fin_m[r] = M;
-          fin_l[r] = L;
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        for (int idx = tid; idx < n_rows * per_row; idx += 128) {
-          const int r = idx / per_row, d = (idx - r * per_row) * 4;
-          const int g = r / p.block_m, m = r - g * p.block_m, pos = mt * p.block_m + m;
-          if (pos >= p.seq_q) continue;
-          float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (int s2 = 0; s2 < p.nsplit; ++s2) {
-            const float wt = wsm[r * p.nsplit + s2];
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(p.ws_acc + (ubase + (int64_t)s2 * p.rows + r) * HD + d));
-            a.x += wt * v.x; a.y += wt * v.y; a.z += wt * v.z; a.w += wt * v.w;
-          }
-          const int head = kvh * p.group + g;
-          if (p.mode == kStreamFused) {
-            const float inv = 1.f / fin_l[r];
-            uint2 pk;
-            pk.x = pack2<BF16>(a.x * inv, a.y * inv);
-            pk.y = pack2<BF16>(a.z * inv, a.w * inv);
-            uint16_t* dst = reinterpret_cast<uint16_t*>(p.o) + b * p.o_sb + (int64_t)head * p.o_sh +
-                            (int64_t)pos * p.o_sm + d;
-            *reinterpret_cast<uint2*>(dst) = pk;
-          } else {
-            const int64_t ro = ((int64_t)b * p.hq + head) * p.seq_q + pos;
-            *reinterpret_cast<float4*>(p.acc_out + ro * HD + d) = a;
-            if (d == 0) {
-              p.m_out[ro] = fin_m[r];
-              p.l_out[ro] = fin_l[r];
-            }
-          }
-        }
-        if (tid == 0) p.ws_cnt[unit] = 0u;  // ready for the next call on this workspace
+    }
+    const int head = kvh * p.group + g;
+    if (p.mode == kStreamFused) {
+      const float inv = 1.f / fl[r];
+      uint2 pk;
+      pk.x = pack2<BF16>(a.x * inv, a.y * inv);
+      pk.y = pack2<BF16>(a.z * inv, a.w * inv);
+      uint16_t* dst =
+          reinterpret_cast<uint16_t*>(p.o) + b * p.o_sb + (int64_t)head * p.o_sh + (int64_t)pos * p.o_sm + d;
+      *reinterpret_cast<uint2*>(dst) = pk;
+    } else {
+      const int64_t ro = ((int64_t)b * p.hq + head) * p.seq_q + pos;
+      *reinterpret_cast<float4*>(p.acc_out + ro * HD + d) = a;
+      if (d == 0) {
+        p.m_out[ro] = fm[r];
+        p.l_out[ro] = fl[r];
       }
     }
   }
+  if (tid == 0) p.ws_cnt[unit] = 0u;  // ready for the next call on this workspace
 }
+
+#undef GQA_CBAR
 
 }  // namespace gqa
