@@ -72,6 +72,22 @@ __device__ __forceinline__ uint32_t mbar_try_wait(uint32_t bar, uint32_t parity)
   return ok;
 }
 
+// As mbar_try_wait, but the warp is suspended in hardware (no issue slots
+// taken from the other warps of its SM sub-partition) until the phase
+// completes or about kSuspendHintNs pass.
+constexpr uint32_t kSuspendHintNs = 1000000;
+__device__ __forceinline__ uint32_t mbar_try_wait_suspend(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return ok;
+}
+
 // Wait for the phase with the given parity to complete. Returns false (after
 // recording `site` in the device error word and raising the CTA-wide abort
 // flag) if it does not complete within kWaitLimitNs, or returns false at once
@@ -82,8 +98,8 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   const uint64_t t0 = globaltimer_ns();
   while (true) {
 #pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
+    for (int i = 0; i < 4; ++i)
+      if (mbar_try_wait_suspend(bar, parity)) return true;
     if (*abort_flag) return false;
     if (globaltimer_ns() - t0 > kWaitLimitNs) {
       *abort_flag = 1;
@@ -248,6 +264,11 @@ __device__ __forceinline__ void reg_fence(uint32_t (&r)[N]) {
 #pragma unroll
   for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
 }
+template <int N>
+__device__ __forceinline__ void reg_fence_n(uint32_t* r) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
+}
 
 // ---------------------------------------------------------------------------
 // Legacy warp-level MMA path (used by the HBM-bound streaming kernel).
@@ -283,6 +304,57 @@ __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Packed two-lane fp32 arithmetic (sm_100: one instruction for two values).
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+// Three-input maximum (one instruction on sm_100).
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for two values on the FMA pipe instead of the MUFU pipe, so the two
+// pipes share the softmax's exponentials. Cody-Waite style range reduction:
+// n = round(x) through the 1.5 * 2^23 addend (n lands in the low mantissa bits
+// of t), f = x - n in [-1/2, 1/2]; 2^f by a degree-3 polynomial fitted for
+// near-equioscillating relative error (csrc/fit_exp2.py; max relative error
+// 1.5e-4, far below the 2^-8 step of the bf16 P it feeds); the result's
+// exponent field then gets n added. x is clamped at -126 so the exponent never
+// underflows into the sign bit; a NaN x (row with no visible key) also lands
+// on the clamp, so callers keep at least one MUFU column per row for NaN rows.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  constexpr float kC0 = 0.9999280571937561f, kC1 = 0.6932609677314758f;
+  constexpr float kC2 = 0.2426111251115799f, kC3 = 0.0551716685295105f;
+  x.x = fmaxf(x.x, -126.0f);
+  x.y = fmaxf(x.y, -126.0f);
+  const float2 t = add2(x, make_float2(kRound, kRound));
+  const float2 n = add2(t, make_float2(-kRound, -kRound));
+  const float2 f = fma2(n, make_float2(-1.0f, -1.0f), x);
+  float2 p = fma2(make_float2(kC3, kC3), f, make_float2(kC2, kC2));
+  p = fma2(p, f, make_float2(kC1, kC1));
+  p = fma2(p, f, make_float2(kC0, kC0));
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
 }
 
 // Pack two floats into one 32-bit register of two 16-bit values (lo = a).

@@ -45,8 +45,8 @@ struct PrefillCfg {
   static constexpr int kQOff = 0;
   static constexpr int kKVOff = 2 * kTileBytes;
   static constexpr int kBarOff = kKVOff + kSlots * kTileBytes;
-  // barriers: q_full[2] kv_full[S] kv_empty[S] s_full[2] p_full[2] o_final[2] mma_done
-  static constexpr int kNumBars = 2 + 2 * kSlots + 2 + 2 + 2 + 1;
+  // barriers: q_full[2] kv_full[S] kv_empty[S] s_full[2] p_full[2 tiles][2 halves] o_final[2] mma_done
+  static constexpr int kNumBars = 2 + 2 * kSlots + 2 + 4 + 2 + 1;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;  // tmem base, abort flag
   static constexpr int kSmemBytes = kMiscOff + 16 + 1024;  // + alignment slack
   // warps 0-3 softmax tile 0, 4-7 softmax tile 1, 8 MMA issuer, 9 TMA producer, 10-11 idle
@@ -59,6 +59,12 @@ struct PrefillCfg {
   static constexpr int kControlRegs = 88;
   static constexpr int kRegsNeeded = 256 * kSoftmaxRegs + 128 * kControlRegs;  // 64512 = 384 x 168
   static constexpr int kColS0 = 0, kColS1 = 128, kColO0 = 256, kColO1 = 256 + HD;
+  // Of every four column pairs of P, this many take the MUFU ex2 and the rest the
+  // polynomial exp2 on the FMA pipe (exp2_poly2): the split that balances the two pipes.
+#ifndef GQA_PREFILL_MUFU_PAIRS_PER4
+#define GQA_PREFILL_MUFU_PAIRS_PER4 3
+#endif
+  static constexpr int kMufuPairsPer4 = GQA_PREFILL_MUFU_PAIRS_PER4;
 };
 
 template <int HD, bool BF16>
@@ -82,8 +88,8 @@ __global__ void __launch_bounds__(384, 1)
   const uint32_t bar_kv_full = bars + 16;                // [SLOTS]
   const uint32_t bar_kv_empty = bar_kv_full + 8 * SLOTS; // [SLOTS]
   const uint32_t bar_s_full = bar_kv_empty + 8 * SLOTS;  // [2]
-  const uint32_t bar_p_full = bar_s_full + 16;           // [2]
-  const uint32_t bar_o_final = bar_p_full + 16;          // [2]
+  const uint32_t bar_p_full = bar_s_full + 16;           // [2][2]: (tile, 64-key half of P)
+  const uint32_t bar_o_final = bar_p_full + 32;          // [2]
   const uint32_t bar_mma_done = bar_o_final + 16;
   uint32_t* tmem_base_ptr = reinterpret_cast<uint32_t*>(smem + Cfg::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kMiscOff + 4);
@@ -113,7 +119,8 @@ __global__ void __launch_bounds__(384, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar_s_full + 8 * i, 1);
-      mbar_init(bar_p_full + 8 * i, 128);
+      mbar_init(bar_p_full + 16 * i, 128);
+      mbar_init(bar_p_full + 16 * i + 8, 128);
       mbar_init(bar_o_final + 8 * i, 1);
     }
     mbar_init(bar_mma_done, 1);
@@ -185,12 +192,14 @@ __global__ void __launch_bounds__(384, 1)
           umma_ss(tS, desc_sw128_kmajor(qa + o), desc_sw128_kmajor(kb + o), idesc_qk, k > 0 ? 1u : 0u);
         }
       };
-      auto issue_pv = [&](int i, int slot, bool acc) {
+      // O_i += P_i V over the 64-key half h of the tile (4 UMMAs of 16 keys each).
+      auto issue_pv = [&](int i, int slot, int h, bool acc) {
         const uint32_t tS = tmem_base + (i ? Cfg::kColS1 : Cfg::kColS0);
         const uint32_t tO = tmem_base + (i ? Cfg::kColO1 : Cfg::kColO0);
         const uint32_t vb = kv_smem0 + slot * Cfg::kTileBytes;
 #pragma unroll
-        for (int k = 0; k < Cfg::kBN / 16; ++k) {
+        for (int kk = 0; kk < Cfg::kBN / 32; ++kk) {
+          const int k = h * (Cfg::kBN / 32) + kk;
           // P: 16 keys = 8 TMEM columns of packed 16-bit pairs; V: 16 key rows of 128 B.
           umma_ts(tO, tS + k * 8, desc_sw128_mnmajor(vb + k * 16 * 128, Cfg::kSubBytes), idesc_pv,
                   (acc || k > 0) ? 1u : 0u);
@@ -211,7 +220,10 @@ __global__ void __launch_bounds__(384, 1)
           if (!mbar_wait(bar_kv_full + 8 * sv, (tv / SLOTS) & 1, abort_flag, 13)) break;
           if (!mbar_wait(bar_p_full, j & 1, abort_flag, 14)) break;
           tc_fence_after();
-          issue_pv(0, sv, j > 0);
+          issue_pv(0, sv, 0, j > 0);
+          if (!mbar_wait(bar_p_full + 8, j & 1, abort_flag, 18)) break;
+          tc_fence_after();
+          issue_pv(0, sv, 1, true);
           const bool more = (j + 1 < nk);
           if (more) {
             if (!mbar_wait(bar_kv_full + 8 * sk, (tk / SLOTS) & 1, abort_flag, 15)) break;
@@ -221,9 +233,12 @@ __global__ void __launch_bounds__(384, 1)
           } else {
             umma_commit(bar_o_final);
           }
-          if (!mbar_wait(bar_p_full + 8, j & 1, abort_flag, 16)) break;
+          if (!mbar_wait(bar_p_full + 16, j & 1, abort_flag, 16)) break;
           tc_fence_after();
-          issue_pv(1, sv, j > 0);
+          issue_pv(1, sv, 0, j > 0);
+          if (!mbar_wait(bar_p_full + 24, j & 1, abort_flag, 19)) break;
+          tc_fence_after();
+          issue_pv(1, sv, 1, true);
           umma_commit(bar_kv_empty + 8 * sv);  // V_j consumed
           if (more) {
             issue_qk(1, sk);
@@ -251,7 +266,7 @@ __global__ void __launch_bounds__(384, 1)
     const uint32_t tS = tmem_base + lane_off + (wg ? Cfg::kColS1 : Cfg::kColS0);
     const uint32_t tO = tmem_base + lane_off + (wg ? Cfg::kColO1 : Cfg::kColO0);
     const uint32_t s_full = bar_s_full + 8 * wg;
-    const uint32_t p_full = bar_p_full + 8 * wg;
+    const uint32_t p_full = bar_p_full + 16 * wg;  // + 8 for the second half
 
     const int g = row / p.bm;
     const int pos = p0 + wg * p.bm + (row - g * p.bm);
@@ -267,26 +282,45 @@ __global__ void __launch_bounds__(384, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
+      // S row: the second half's TMEM load is in flight while the first half's max
+      // is computed (the partial maxima feed the second wait, so they precede it).
       uint32_t sr[128];
       tmem_ld32(tS + 0, sr + 0);
       tmem_ld32(tS + 32, sr + 32);
+      tmem_wait_ld();
+      reg_fence_n<64>(sr);
       tmem_ld32(tS + 64, sr + 64);
       tmem_ld32(tS + 96, sr + 96);
-      tmem_wait_ld();
-      reg_fence(sr);
       const int rem = lim - j * Cfg::kBN;  // visible columns in this tile
-      if (rem < Cfg::kBN) {
+      const bool masked = rem < Cfg::kBN;
+      if (masked) {
 #pragma unroll
-        for (int c = 0; c < 128; ++c) sr[c] = (c < rem) ? sr[c] : __float_as_uint(-INFINITY);
+        for (int c = 0; c < 64; ++c) sr[c] = (c < rem) ? sr[c] : __float_as_uint(-INFINITY);
       }
+      // Row max with three-input maxima, four independent chains.
       float mx0 = __uint_as_float(sr[0]), mx1 = __uint_as_float(sr[1]);
       float mx2 = __uint_as_float(sr[2]), mx3 = __uint_as_float(sr[3]);
 #pragma unroll
-      for (int c = 4; c < 128; c += 4) {
-        mx0 = fmaxf(mx0, __uint_as_float(sr[c]));
-        mx1 = fmaxf(mx1, __uint_as_float(sr[c + 1]));
-        mx2 = fmaxf(mx2, __uint_as_float(sr[c + 2]));
-        mx3 = fmaxf(mx3, __uint_as_float(sr[c + 3]));
+      for (int c = 4; c < 60; c += 8) {
+        mx0 = max3(mx0, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+        mx1 = max3(mx1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
+        mx2 = max3(mx2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
+        mx3 = max3(mx3, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
+      }
+      mx0 = max3(mx0, __uint_as_float(sr[60]), __uint_as_float(sr[61]));
+      mx1 = max3(mx1, __uint_as_float(sr[62]), __uint_as_float(sr[63]));
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::"f"(mx0), "f"(mx1), "f"(mx2), "f"(mx3) : "memory");
+      reg_fence_n<64>(sr + 64);
+      if (masked) {
+#pragma unroll
+        for (int c = 64; c < 128; ++c) sr[c] = (c < rem) ? sr[c] : __float_as_uint(-INFINITY);
+      }
+#pragma unroll
+      for (int c = 64; c < 128; c += 8) {
+        mx0 = max3(mx0, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+        mx1 = max3(mx1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
+        mx2 = max3(mx2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
+        mx3 = max3(mx3, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
       }
       const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * scale;
       const float m_new = fmaxf(m_run, mx);
@@ -309,25 +343,39 @@ __global__ void __launch_bounds__(384, 1)
         l_run *= fast_exp2(m_run - m_new);
         m_run = m_new;
       }
-      const float nm = -m_run;
-      float sum0 = 0.f, sum1 = 0.f;
+      // P = exp2(S * scale - m), written over S as packed 16-bit pairs, in two 64-key
+      // halves so the PV MMAs of the first half start while the second is computed.
+      // One column pair in four takes the polynomial exp2 on the FMA pipe, the rest
+      // the MUFU ex2; the row sum and the scale use packed two-lane fp32 math.
+      const float2 sc2 = make_float2(scale, scale);
+      const float2 nm2 = make_float2(-m_run, -m_run);
+      float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t pk[16];
+      for (int h = 0; h < 2; ++h) {
+        uint32_t pk[32];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const float a = fast_exp2(fmaf(__uint_as_float(sr[32 * c + 2 * e]), scale, nm));
-          const float bb = fast_exp2(fmaf(__uint_as_float(sr[32 * c + 2 * e + 1]), scale, nm));
-          sum0 += a;
-          sum1 += bb;
-          pk[e] = pack2<BF16>(a, bb);
+        for (int c = 0; c < 32; ++c) {
+          const int col = 64 * h + 2 * c;
+          const float2 x = fma2(make_float2(__uint_as_float(sr[col]), __uint_as_float(sr[col + 1])), sc2, nm2);
+          float2 pv;
+          if ((c & 3) >= Cfg::kMufuPairsPer4) {
+            pv = exp2_poly2(x);
+          } else {
+            pv.x = fast_exp2(x.x);
+            pv.y = fast_exp2(x.y);
+          }
+          sum2[c & 3] = add2(sum2[c & 3], pv);
+          pk[c] = pack2<BF16>(pv.x, pv.y);
         }
-        tmem_st16(tS + c * 16, pk);
+        tmem_st32(tS + 32 * h, pk);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(p_full + 8 * h);
       }
-      l_run += sum0 + sum1;
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(p_full);
+      const float2 s01 = add2(sum2[0], sum2[1]);
+      const float2 s23 = add2(sum2[2], sum2[3]);
+      const float2 st = add2(s01, s23);
+      l_run += st.x + st.y;
     }
 
     // ---- epilogue: O / l -> 16-bit -> swizzled staging (this tile's Q buffer) -> TMA store
