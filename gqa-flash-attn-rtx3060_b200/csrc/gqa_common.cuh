@@ -339,8 +339,10 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
 // near-equioscillating relative error (csrc/fit_exp2.py; max relative error
 // 1.5e-4, far below the 2^-8 step of the bf16 P it feeds); the result's
 // exponent field then gets n added. x is clamped at -126 so the exponent never
-// underflows into the sign bit; a NaN x (row with no visible key) also lands
-// on the clamp, so callers keep at least one MUFU column per row for NaN rows.
+// underflows into the sign bit: x < -126 (masked keys, -inf) gives about 1e-38
+// instead of 0, negligible against any visible key; a NaN x (row with no visible
+// key) also lands on the clamp, so callers keep MUFU columns in every row for the
+// NaN to propagate.
 __device__ __forceinline__ float2 exp2_poly2(float2 x) {
   constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
   constexpr float kC0 = 0.9999280571937561f, kC1 = 0.6932609677314758f;

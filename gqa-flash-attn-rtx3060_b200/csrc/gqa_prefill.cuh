@@ -32,7 +32,49 @@ struct PrefillParams {
   int n_pairs;  // ceil(ceil(seq_q / bm) / 2)
   int causal;
   float scale_log2;
+  // Key-axis split of each unit (query pair of one (batch, kv head)) across
+  // nsplit CTAs of chunk_tiles key tiles each; 1 = no split. Split CTAs publish
+  // fp32 partials [unit][split][256 rows] (m, l, acc[HD]) and the last CTA of the
+  // unit (atomic ticket ws_cnt[unit], zero between calls) combines them.
+  int nsplit;
+  int chunk_tiles;
+  float* ws_m;
+  float* ws_l;
+  float* ws_acc;
+  unsigned* ws_cnt;
 };
+
+// Work item of CTA `cta`: unit = (query pair, batch, kv head), longest pair first;
+// split = which chunk of the unit's key tiles. A unit with fewer key tiles than
+// the splits cover uses fewer splits (n_valid); the others return at once.
+struct PrefillWork {
+  int unit, split, n_valid, b, kvh, p0, j0, nk;
+};
+
+template <int BN, bool SPLIT>
+__device__ __forceinline__ PrefillWork prefill_work(const PrefillParams& p, unsigned cta) {
+  // The integer forms below (unsigned division of the CTA index, signed after it)
+  // are the ones under which the unsplit instantiation compiles without register
+  // spills at the 208-register softmax budget; recheck `-Xptxas -v` after changes.
+  PrefillWork w;
+  const unsigned unit = SPLIT ? cta / (unsigned)p.nsplit : cta;
+  w.split = SPLIT ? (int)(cta % (unsigned)p.nsplit) : 0;
+  w.unit = (int)unit;
+  const int bh_count = p.batch * p.hkv;
+  const int bh = unit % bh_count;
+  const int pair = p.n_pairs - 1 - unit / bh_count;
+  w.b = bh / p.hkv;
+  w.kvh = bh % p.hkv;
+  w.p0 = pair * 2 * p.bm;  // first position of tile 0
+  const int off = p.seq_kv - p.seq_q;
+  int kv_end = p.seq_kv;
+  if (p.causal) kv_end = min(kv_end, min(w.p0 + 2 * p.bm, p.seq_q) + off);
+  const int nk_unit = (kv_end > 0) ? (kv_end + BN - 1) / BN : 0;
+  w.n_valid = SPLIT ? max(1, (nk_unit + p.chunk_tiles - 1) / p.chunk_tiles) : 1;
+  w.j0 = (SPLIT && w.n_valid > 1) ? w.split * p.chunk_tiles : 0;  // key tiles [j0, j0 + nk)
+  w.nk = (SPLIT && w.n_valid > 1) ? min(nk_unit, w.j0 + p.chunk_tiles) - w.j0 : nk_unit;
+  return w;
+}
 
 template <int HD>
 struct PrefillCfg {
@@ -67,7 +109,7 @@ struct PrefillCfg {
   static constexpr int kMufuPairsPer4 = GQA_PREFILL_MUFU_PAIRS_PER4;
 };
 
-template <int HD, bool BF16>
+template <int HD, bool BF16, bool SPLIT>
 __global__ void __launch_bounds__(384, 1)
     gqa_prefill_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap qmap,
                        const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
@@ -99,16 +141,10 @@ __global__ void __launch_bounds__(384, 1)
   const int lane = tid & 31;
 
   // ---- work item: longest (highest) query pair first, across all (b, kv) ----
-  const int bh_count = p.batch * p.hkv;
-  const int bh = blockIdx.x % bh_count;
-  const int pair = p.n_pairs - 1 - blockIdx.x / bh_count;
-  const int b = bh / p.hkv;
-  const int kvh = bh % p.hkv;
-  const int p0 = pair * 2 * p.bm;  // first position of tile 0
+  const PrefillWork wk = prefill_work<Cfg::kBN, SPLIT>(p, blockIdx.x);
+  if (wk.split >= wk.n_valid) return;  // whole CTA, before any barrier or TMEM use
+  const int b = wk.b, kvh = wk.kvh, p0 = wk.p0, j0 = wk.j0, nk = wk.nk;
   const int off = p.seq_kv - p.seq_q;
-  int kv_end = p.seq_kv;
-  if (p.causal) kv_end = min(kv_end, min(p0 + 2 * p.bm, p.seq_q) + off);
-  const int nk = (kv_end > 0) ? (kv_end + Cfg::kBN - 1) / Cfg::kBN : 0;
 
   if (tid == 0) {
     mbar_init(bar_q_full, 1);
@@ -166,7 +202,7 @@ __global__ void __launch_bounds__(384, 1)
         const uint32_t full = bar_kv_full + 8 * slot;
         mbar_arrive_expect_tx(full, Cfg::kTileBytes);
         const CUtensorMap* map = (t & 1) ? &vmap : &kmap;
-        const int key0 = (t >> 1) * Cfg::kBN;
+        const int key0 = (j0 + (t >> 1)) * Cfg::kBN;
 #pragma unroll
         for (int s = 0; s < NSUB; ++s)
           tma_load_4d(kv_smem0 + slot * Cfg::kTileBytes + s * Cfg::kSubBytes, map, full, s * 64, key0, kvh, b);
@@ -272,9 +308,16 @@ __global__ void __launch_bounds__(384, 1)
     const int pos = p0 + wg * p.bm + (row - g * p.bm);
     int lim = p.seq_kv;  // number of keys this row may see
     if (p.causal) lim = min(lim, pos + off + 1);
+    lim -= j0 * Cfg::kBN;  // counted from this CTA's first key tile
     const float scale = p.scale_log2;
 
-    float m_run = -INFINITY;
+    // A row that sees no key at all keeps m = -inf, and its NaN (exp2(-inf + inf))
+    // reaches the output, as in the reference. Such rows only occur in units of at
+    // most two key tiles, which are never split. In a split unit a row may see no
+    // key of this CTA's chunk while it sees keys of others: a finite start value
+    // keeps its P finite (exp2(-inf + 3e38) = 0), and the combine gives the chunk
+    // the weight exp2(-3e38 - M) = 0.
+    float m_run = (wk.n_valid > 1) ? -3.0e38f : -INFINITY;
     float l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < nk; ++j) {
@@ -385,7 +428,79 @@ __global__ void __launch_bounds__(384, 1)
       have_o = __all_sync(0xffffffffu, have_o);
     }
     if (have_o) tc_fence_after();
-    const float inv = 1.0f / l_run;  // l == 0 -> inf -> NaN rows, as the reference's 0/0
+
+    // Key-split unit: publish this CTA's partial; the last CTA of the unit folds
+    // the other splits' partials into its own before the store below. The work item
+    // is derived again from a fresh read of the CTA index, so none of its fields
+    // stays live in registers across the softmax loop.
+    int unit = 0, split = 0, n_valid = 1;
+    if constexpr (SPLIT) {
+      unsigned cta;
+      asm volatile("mov.u32 %0, %%ctaid.x;" : "=r"(cta));
+      const PrefillWork wk2 = prefill_work<Cfg::kBN, SPLIT>(p, cta);
+      unit = wk2.unit;
+      split = wk2.split;
+      n_valid = wk2.n_valid;
+    }
+    float w_own = 1.0f, inv = 1.0f / l_run;  // l == 0 -> inf -> NaN rows, the reference's 0/0
+    float m_ref = 0.f;                       // reference max of the combined splits
+    bool store = true;
+    int n_other = 0;
+    const int prow = wg * 128 + row;  // row of the unit's 256 packed rows
+    const int64_t pbase = ((int64_t)unit * p.nsplit) * 256;
+    if (n_valid > 1) {
+      const int64_t mine = pbase + (int64_t)split * 256 + prow;
+      __stcg(p.ws_m + mine, m_run);
+      __stcg(p.ws_l + mine, l_run);
+#pragma unroll
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t orr[32];
+        if (have_o) {
+          tmem_ld32(tO + c * 32, orr);
+          tmem_wait_ld();
+          reg_fence(orr);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) orr[e] = __float_as_uint(__int_as_float(0x7fc00000));
+        }
+        float4* dst = reinterpret_cast<float4*>(p.ws_acc + mine * HD + c * 32);
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          __stcg(dst + e, make_float4(__uint_as_float(orr[4 * e]), __uint_as_float(orr[4 * e + 1]),
+                                      __uint_as_float(orr[4 * e + 2]), __uint_as_float(orr[4 * e + 3])));
+      }
+      // Both softmax warpgroups have published; thread 0's release-acquire ticket
+      // (fences are cumulative) tells whether this CTA is the unit's last.
+      asm volatile("bar.sync 3, 256;" ::: "memory");
+      uint32_t* last_slot = tmem_base_ptr + 2;
+      if (tid == 0) {
+        unsigned ticket;
+        asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(ticket) : "l"(p.ws_cnt + unit)
+                     : "memory");
+        const bool last = ticket == (unsigned)(n_valid - 1);
+        *last_slot = last ? 1u : 0u;
+        if (last) p.ws_cnt[unit] = 0u;  // every split has arrived: ready for the next call
+      }
+      asm volatile("bar.sync 3, 256;" ::: "memory");
+      store = *last_slot != 0;
+      if (store) {
+        // Combined weights of this row over the splits: w_s = exp2(m_s - max m).
+        float M = m_run;
+        for (int s2 = 0; s2 < n_valid; ++s2)
+          if (s2 != split) M = fmaxf(M, __ldcg(p.ws_m + pbase + (int64_t)s2 * 256 + prow));
+        const float Mu = (M == -INFINITY) ? 0.f : M;
+        w_own = fast_exp2(m_run - Mu);
+        float L = w_own * l_run;
+        for (int s2 = 0; s2 < n_valid; ++s2)
+          if (s2 != split) {
+            const int64_t o2 = pbase + (int64_t)s2 * 256 + prow;
+            L += fast_exp2(__ldcg(p.ws_m + o2) - Mu) * __ldcg(p.ws_l + o2);
+          }
+        inv = 1.0f / L;
+        n_other = n_valid - 1;
+        m_ref = Mu;
+      }
+    }
     const uint32_t stage = q_smem0 + wg * Cfg::kTileBytes;
 #pragma unroll
     for (int c = 0; c < HD / 32; ++c) {
@@ -397,6 +512,24 @@ __global__ void __launch_bounds__(384, 1)
       } else {
 #pragma unroll
         for (int e = 0; e < 32; ++e) orr[e] = __float_as_uint(__int_as_float(0x7fc00000));
+      }
+      if (n_other > 0) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) orr[e] = __float_as_uint(w_own * __uint_as_float(orr[e]));
+        for (int s2 = 0; s2 < n_valid; ++s2) {
+          if (s2 == split) continue;
+          const int64_t o2 = pbase + (int64_t)s2 * 256 + prow;
+          const float w = fast_exp2(__ldcg(p.ws_m + o2) - m_ref);
+          const float4* src = reinterpret_cast<const float4*>(p.ws_acc + o2 * HD + c * 32);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float4 v4 = __ldcg(src + e);
+            orr[4 * e] = __float_as_uint(fmaf(w, v4.x, __uint_as_float(orr[4 * e])));
+            orr[4 * e + 1] = __float_as_uint(fmaf(w, v4.y, __uint_as_float(orr[4 * e + 1])));
+            orr[4 * e + 2] = __float_as_uint(fmaf(w, v4.z, __uint_as_float(orr[4 * e + 2])));
+            orr[4 * e + 3] = __float_as_uint(fmaf(w, v4.w, __uint_as_float(orr[4 * e + 3])));
+          }
+        }
       }
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -418,7 +551,7 @@ __global__ void __launch_bounds__(384, 1)
     else
       asm volatile("bar.sync 2, 128;" ::: "memory");
     const int tile_pos = p0 + wg * p.bm;
-    if (row == 0 && tile_pos < p.seq_q) {
+    if (store && row == 0 && tile_pos < p.seq_q) {
 #pragma unroll
       for (int s = 0; s < NSUB; ++s)
         tma_store_4d(&omap, stage + s * Cfg::kSubBytes, s * 64, tile_pos, kvh * p.group, b);

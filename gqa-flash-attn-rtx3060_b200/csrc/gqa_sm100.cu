@@ -61,15 +61,19 @@ int init_device(int dev) {
   }
   cudaError_t e = cudaSuccess;
   auto chk = [&](cudaError_t x) { if (x != cudaSuccess && e == cudaSuccess) e = x; };
-  chk(set_smem(gqa_prefill_kernel<128, true>, PrefillCfg<128>::kSmemBytes));
-  chk(set_smem(gqa_prefill_kernel<128, false>, PrefillCfg<128>::kSmemBytes));
-  chk(set_smem(gqa_prefill_kernel<64, true>, PrefillCfg<64>::kSmemBytes));
-  chk(set_smem(gqa_prefill_kernel<64, false>, PrefillCfg<64>::kSmemBytes));
+  int rs = GQA_OK;
+  // Both key-split instantiations of each (head_dim, dtype): shared memory opt-in,
+  // and the setmaxnreg split must fit the registers the launch holds.
+#define GQA_PREP_PREFILL(HD, BF, SP)                                                      \
+  chk(set_smem(gqa_prefill_kernel<HD, BF, SP>, PrefillCfg<HD>::kSmemBytes));              \
+  if (!rs) rs = check_reg_split(gqa_prefill_kernel<HD, BF, SP>, PrefillCfg<HD>::kThreads, \
+                                PrefillCfg<HD>::kRegsNeeded)
+  GQA_PREP_PREFILL(128, true, false); GQA_PREP_PREFILL(128, false, false);
+  GQA_PREP_PREFILL(64, true, false); GQA_PREP_PREFILL(64, false, false);
+  GQA_PREP_PREFILL(128, true, true); GQA_PREP_PREFILL(128, false, true);
+  GQA_PREP_PREFILL(64, true, true); GQA_PREP_PREFILL(64, false, true);
+#undef GQA_PREP_PREFILL
   if (e != cudaSuccess) return GQA_ERR_CUDA;
-  int rs = check_reg_split(gqa_prefill_kernel<128, true>, PrefillCfg<128>::kThreads, PrefillCfg<128>::kRegsNeeded);
-  if (!rs) rs = check_reg_split(gqa_prefill_kernel<128, false>, PrefillCfg<128>::kThreads, PrefillCfg<128>::kRegsNeeded);
-  if (!rs) rs = check_reg_split(gqa_prefill_kernel<64, true>, PrefillCfg<64>::kThreads, PrefillCfg<64>::kRegsNeeded);
-  if (!rs) rs = check_reg_split(gqa_prefill_kernel<64, false>, PrefillCfg<64>::kThreads, PrefillCfg<64>::kRegsNeeded);
   if (rs) return rs;
 #define GQA_SET_STREAM(HD, BF, RG) chk(set_smem(gqa_stream_kernel<HD, BF, RG>, StreamCfg<HD>::kSmemBytes))
   GQA_SET_STREAM(128, true, 1); GQA_SET_STREAM(128, true, 2); GQA_SET_STREAM(128, true, 4);
@@ -216,6 +220,54 @@ void stream_ws_carve(const StreamPlan& pl, int head_dim, void* ws, StreamParams*
 
 bool use_stream(const Shape& s) { return s.group <= kStreamMaxRows && s.group * s.seq_q <= kStreamMaxRows; }
 
+// ----------------------------------------------------------------------------- prefill plan
+// Units are query pairs (2 x 128 packed rows) of one (batch, kv head). When they
+// are fewer than the SMs (short query blocks against long keys, or a GPU's share
+// of a sharded batch), each unit's key tiles are split across CTAs so every SM
+// gets work; the partials are combined by the unit's last CTA.
+struct PrefillPlan {
+  int bm, n_pairs, units, nsplit, chunk_tiles;
+};
+
+PrefillPlan plan_prefill(const Shape& s, int sm_count) {
+  PrefillPlan pl{};
+  pl.bm = 128 / s.group;
+  const int n_tiles = (s.seq_q + pl.bm - 1) / pl.bm;
+  pl.n_pairs = (n_tiles + 1) / 2;
+  pl.units = pl.n_pairs * s.batch * s.hkv;
+  pl.nsplit = 1;
+  pl.chunk_tiles = 0;
+  const int nk_max = (s.seq_kv + 127) / 128;
+  if (pl.units > 0 && pl.units < sm_count) {
+    int ns = std::min(sm_count / pl.units, 16);
+    while (ns > 1 && nk_max < 2 * ns) --ns;  // at least two key tiles per split
+    if (ns > 1) {
+      pl.nsplit = ns;
+      pl.chunk_tiles = (nk_max + ns - 1) / ns;
+    }
+  }
+  return pl;
+}
+
+size_t prefill_ws_bytes(const PrefillPlan& pl, int head_dim) {
+  if (pl.nsplit <= 1) return 0;
+  const size_t rows = (size_t)pl.units * pl.nsplit * 256;
+  return align256((size_t)pl.units * 4) + 2 * align256(rows * 4) + align256(rows * head_dim * 4);
+}
+
+void prefill_ws_carve(const PrefillPlan& pl, int head_dim, void* ws, PrefillParams* p) {
+  const size_t rows = (size_t)pl.units * pl.nsplit * 256;
+  uint8_t* c = reinterpret_cast<uint8_t*>(ws);
+  p->ws_cnt = reinterpret_cast<unsigned*>(c);
+  c += align256((size_t)pl.units * 4);
+  p->ws_m = reinterpret_cast<float*>(c);
+  c += align256(rows * 4);
+  p->ws_l = reinterpret_cast<float*>(c);
+  c += align256(rows * 4);
+  p->ws_acc = reinterpret_cast<float*>(c);
+  (void)head_dim;
+}
+
 template <int HD, bool BF>
 cudaError_t launch_stream_hd(const StreamParams& p, const StreamPlan& pl, const CUtensorMap& km,
                              const CUtensorMap& vm, cudaStream_t st) {
@@ -310,9 +362,10 @@ int gqa_sm_count(void) {
 size_t gqa_fwd_workspace_bytes(int batch, int num_heads, int num_kv_heads, int seq_q, int seq_kv, int head_dim) {
   Shape s;
   if (check_shape(batch, num_heads, num_kv_heads, seq_q, seq_kv, head_dim, &s)) return 0;
-  if (!use_stream(s) || seq_q == 0 || seq_kv == 0 || batch == 0) return 0;
+  if (seq_q == 0 || seq_kv == 0 || batch == 0) return 0;
   int sm = 0;
   if (current_device(&sm)) return 0;
+  if (!use_stream(s)) return prefill_ws_bytes(plan_prefill(s, sm), head_dim);
   const StreamPlan pl = plan_stream(s, sm, true);
   return pl.nsplit > 1 ? stream_ws_bytes(pl, head_dim) : 0;
 }
@@ -359,6 +412,11 @@ int gqa_fwd(const void* q, const void* k, const void* v, void* o, const int64_t*
   }
 
   // tcgen05 prefill path
+  PrefillPlan pp = plan_prefill(s, sm);
+  if (pp.nsplit > 1 && (!workspace || workspace_bytes < prefill_ws_bytes(pp, head_dim) || !aligned16(workspace))) {
+    pp.nsplit = 1;  // no room for the partials: one CTA per unit
+    pp.chunk_tiles = 0;
+  }
   PrefillParams p{};
   p.batch = batch;
   p.hq = num_heads;
@@ -366,31 +424,33 @@ int gqa_fwd(const void* q, const void* k, const void* v, void* o, const int64_t*
   p.group = s.group;
   p.seq_q = seq_q;
   p.seq_kv = seq_kv;
-  p.bm = 128 / s.group;
-  const int n_tiles = (seq_q + p.bm - 1) / p.bm;
-  p.n_pairs = (n_tiles + 1) / 2;
+  p.bm = pp.bm;
+  p.n_pairs = pp.n_pairs;
   p.causal = causal ? 1 : 0;
   p.scale_log2 = scale_log2;
+  p.nsplit = pp.nsplit;
+  p.chunk_tiles = pp.chunk_tiles;
+  if (pp.nsplit > 1) prefill_ws_carve(pp, head_dim, workspace, &p);
   CUtensorMap qm, km, vm, om;
   rc = make_map(&qm, q, qs, batch, num_heads, seq_q, head_dim, p.bm, s.group);
   if (!rc) rc = make_map(&km, k, ks, batch, num_kv_heads, seq_kv, head_dim, 128, 1);
   if (!rc) rc = make_map(&vm, v, vs, batch, num_kv_heads, seq_kv, head_dim, 128, 1);
   if (!rc) rc = make_map(&om, o, os, batch, num_heads, seq_q, head_dim, p.bm, s.group);
   if (rc) return rc;
-  const int64_t grid = (int64_t)p.n_pairs * batch * num_kv_heads;
+  const int64_t grid = (int64_t)p.n_pairs * batch * num_kv_heads * p.nsplit;
   if (grid > 0x7fffffff) return GQA_ERR_INVALID_ARG;
   const bool bf = dtype == GQA_DTYPE_BF16;
+  const bool split = p.nsplit > 1;  // the unsplit instantiation carries no split code
+#define GQA_LAUNCH_PREFILL(HD, BF, SP) \
+  gqa_prefill_kernel<HD, BF, SP><<<(unsigned)grid, PrefillCfg<HD>::kThreads, PrefillCfg<HD>::kSmemBytes, st>>>(p, qm, km, vm, om)
   if (head_dim == 128) {
-    if (bf)
-      gqa_prefill_kernel<128, true><<<(unsigned)grid, PrefillCfg<128>::kThreads, PrefillCfg<128>::kSmemBytes, st>>>(p, qm, km, vm, om);
-    else
-      gqa_prefill_kernel<128, false><<<(unsigned)grid, PrefillCfg<128>::kThreads, PrefillCfg<128>::kSmemBytes, st>>>(p, qm, km, vm, om);
+    if (bf) { if (split) GQA_LAUNCH_PREFILL(128, true, true); else GQA_LAUNCH_PREFILL(128, true, false); }
+    else { if (split) GQA_LAUNCH_PREFILL(128, false, true); else GQA_LAUNCH_PREFILL(128, false, false); }
   } else {
-    if (bf)
-      gqa_prefill_kernel<64, true><<<(unsigned)grid, PrefillCfg<128>::kThreads, PrefillCfg<64>::kSmemBytes, st>>>(p, qm, km, vm, om);
-    else
-      gqa_prefill_kernel<64, false><<<(unsigned)grid, PrefillCfg<128>::kThreads, PrefillCfg<64>::kSmemBytes, st>>>(p, qm, km, vm, om);
+    if (bf) { if (split) GQA_LAUNCH_PREFILL(64, true, true); else GQA_LAUNCH_PREFILL(64, true, false); }
+    else { if (split) GQA_LAUNCH_PREFILL(64, false, true); else GQA_LAUNCH_PREFILL(64, false, false); }
   }
+#undef GQA_LAUNCH_PREFILL
   return launch_status();
 }
 

@@ -51,7 +51,8 @@ def _rank_main(rank, world, port, q_ret):
         br, hr = S.shard_units(B, Hkv, world, rank)
         ql, kl, vl = S.slice_units(q, k, v, br, hr)
         g = Hq // Hkv
-        res["units"] = bool(torch.equal(S.head_sharded_forward(ql, kl, vl), full[br[0]:br[1], hr[0] * g:hr[1] * g]))
+        d = (S.head_sharded_forward(ql, kl, vl).float() - full[br[0]:br[1], hr[0] * g:hr[1] * g].float()).abs()
+        res["units"] = (d.max().item(), d.mean().item())
         dist.barrier()
         q_ret.put((rank, res))
     finally:
@@ -74,7 +75,6 @@ def test_sharded_paths_over_nccl():
     for p in procs:
         p.join(timeout=60)
     for rank, res in results.items():
-        for key in ("seq", "seq_causal"):
+        for key in ("seq", "seq_causal", "units"):
             mx, mn = res[key]
             assert mx < BASELINE_TOL[0] and mn < BASELINE_TOL[1], (rank, key, mx, mn)
-        assert res["units"], rank

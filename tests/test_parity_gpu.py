@@ -134,6 +134,11 @@ EDGE = [
     (1, 8, 2, 65, 65, 64, True),
     (1, 8, 2, 300, 100, 128, True),     # seq_q > seq_kv: top rows see no key -> NaN
     (1, 8, 2, 5, 2, 64, True),          # seq_q > seq_kv, streaming kernel
+    # few query pairs against long keys: the tcgen05 kernel splits each unit's key
+    # tiles across CTAs and the unit's last CTA combines the partials
+    (4, 4, 1, 512, 16384, 128, True),   # one GPU's share of config 4 at 8 GPUs (4 splits)
+    (2, 8, 2, 300, 2000, 128, True),    # causal chunks past some rows' diagonal
+    (1, 8, 1, 200, 3000, 64, False),    # non-causal, head_dim 64
 ]
 
 

@@ -54,5 +54,6 @@ def test_head_sharded_units(world):
         br, hr = S.shard_units(B, Hkv, world, r)
         ql, kl, vl = S.slice_units(q, k, v, br, hr)
         stitched[br[0]:br[1], hr[0] * g:hr[1] * g] = S.head_sharded_forward(ql, kl, vl)
-    # same kernels, same tiles: the unit results do not depend on the sharding
-    assert torch.equal(stitched, full)
+    # A GPU's share has fewer units, so its launch may split key tiles across CTAs
+    # (a different summation order): equal within the contract, not bit for bit.
+    compare(to_np(stitched), to_np(full), BASELINE_TOL)
