@@ -85,12 +85,12 @@ def measured_peaks():
 
 
 def profile_traffic(kernel_key):
-    """Per-launch DRAM bytes of a kernel from a committed ncu summary (profiles/*.txt), or None."""
+    """Per-launch DRAM bytes of a kernel from a committed ncu summary (profiles/*.md|txt), or None."""
     pdir = os.path.join(ROOT, "profiles")
     if not os.path.isdir(pdir):
         return None
     for fn in sorted(os.listdir(pdir)):
-        if not fn.endswith(".txt"):
+        if not fn.endswith((".txt", ".md")):
             continue
         with open(os.path.join(pdir, fn)) as f:
             for line in f:
