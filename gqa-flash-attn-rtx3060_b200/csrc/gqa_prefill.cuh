@@ -34,7 +34,8 @@ struct PrefillParams {
   float scale_log2;
   // Key-axis split of each unit (query pair of one (batch, kv head)) across
   // nsplit CTAs of chunk_tiles key tiles each; 1 = no split. Split CTAs publish
-  // fp32 partials [unit][split][256 rows] (m, l, acc[HD]) and the last CTA of the
+  // fp32 partials m, l [unit][split][256 rows] and acc [unit][split][HD][256 rows]
+  // (row fastest, so a warp's accesses coalesce), and the last CTA of the
   // unit (atomic ticket ws_cnt[unit], zero between calls) combines them.
   int nsplit;
   int chunk_tiles;
@@ -446,12 +447,14 @@ __global__ void __launch_bounds__(384, 1)
     float m_ref = 0.f;                       // reference max of the combined splits
     bool store = true;
     int n_other = 0;
+    // Partials of the unit: m, l [split][256 rows] and acc [split][d][256 rows]; a
+    // warp's 32 rows are consecutive, so every access below is one 128-byte line.
     const int prow = wg * 128 + row;  // row of the unit's 256 packed rows
-    const int64_t pbase = ((int64_t)unit * p.nsplit) * 256;
+    const int64_t pbase = ((int64_t)unit * p.nsplit) * 256 + prow;
     if (n_valid > 1) {
-      const int64_t mine = pbase + (int64_t)split * 256 + prow;
-      __stcg(p.ws_m + mine, m_run);
-      __stcg(p.ws_l + mine, l_run);
+      __stcg(p.ws_m + pbase + (int64_t)split * 256, m_run);
+      __stcg(p.ws_l + pbase + (int64_t)split * 256, l_run);
+      float* acc_own = p.ws_acc + ((int64_t)unit * p.nsplit + split) * HD * 256 + prow;
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t orr[32];
@@ -463,11 +466,8 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
           for (int e = 0; e < 32; ++e) orr[e] = __float_as_uint(__int_as_float(0x7fc00000));
         }
-        float4* dst = reinterpret_cast<float4*>(p.ws_acc + mine * HD + c * 32);
 #pragma unroll
-        for (int e = 0; e < 8; ++e)
-          __stcg(dst + e, make_float4(__uint_as_float(orr[4 * e]), __uint_as_float(orr[4 * e + 1]),
-                                      __uint_as_float(orr[4 * e + 2]), __uint_as_float(orr[4 * e + 3])));
+        for (int e = 0; e < 32; ++e) __stcg(acc_own + (c * 32 + e) * 256, __uint_as_float(orr[e]));
       }
       // Both softmax warpgroups have published; thread 0's release-acquire ticket
       // (fences are cumulative) tells whether this CTA is the unit's last.
@@ -484,18 +484,33 @@ __global__ void __launch_bounds__(384, 1)
       asm volatile("bar.sync 3, 256;" ::: "memory");
       store = *last_slot != 0;
       if (store) {
-        // Combined weights of this row over the splits: w_s = exp2(m_s - max m).
+        // Combined weights of this row over the splits: w_s = exp2(m_s - max m). The
+        // other splits' m and l are read four at a time (clamped indices, own split
+        // and indices past the last masked out) so their latencies overlap.
         float M = m_run;
-        for (int s2 = 0; s2 < n_valid; ++s2)
-          if (s2 != split) M = fmaxf(M, __ldcg(p.ws_m + pbase + (int64_t)s2 * 256 + prow));
+        for (int s0 = 0; s0 < n_valid; s0 += 4) {
+          float mv[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) mv[i] = __ldcg(p.ws_m + pbase + (int64_t)min(s0 + i, n_valid - 1) * 256);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            if (s0 + i < n_valid && s0 + i != split) M = fmaxf(M, mv[i]);
+        }
         const float Mu = (M == -INFINITY) ? 0.f : M;
         w_own = fast_exp2(m_run - Mu);
         float L = w_own * l_run;
-        for (int s2 = 0; s2 < n_valid; ++s2)
-          if (s2 != split) {
-            const int64_t o2 = pbase + (int64_t)s2 * 256 + prow;
-            L += fast_exp2(__ldcg(p.ws_m + o2) - Mu) * __ldcg(p.ws_l + o2);
+        for (int s0 = 0; s0 < n_valid; s0 += 4) {
+          float mv[4], lv[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int64_t o2 = pbase + (int64_t)min(s0 + i, n_valid - 1) * 256;
+            mv[i] = __ldcg(p.ws_m + o2);
+            lv[i] = __ldcg(p.ws_l + o2);
           }
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            if (s0 + i < n_valid && s0 + i != split) L += fast_exp2(mv[i] - Mu) * lv[i];
+        }
         inv = 1.0f / L;
         n_other = n_valid - 1;
         m_ref = Mu;
@@ -516,19 +531,24 @@ __global__ void __launch_bounds__(384, 1)
       if (n_other > 0) {
 #pragma unroll
         for (int e = 0; e < 32; ++e) orr[e] = __float_as_uint(w_own * __uint_as_float(orr[e]));
-        for (int s2 = 0; s2 < n_valid; ++s2) {
-          if (s2 == split) continue;
-          const int64_t o2 = pbase + (int64_t)s2 * 256 + prow;
-          const float w = fast_exp2(__ldcg(p.ws_m + o2) - m_ref);
-          const float4* src = reinterpret_cast<const float4*>(p.ws_acc + o2 * HD + c * 32);
+        // Two other splits per pass: 64 independent loads in flight per thread. An index
+        // past the last split or equal to this CTA's own reads a valid partial at weight 0.
+        for (int s0 = 0; s0 < n_valid; s0 += 2) {
+          const int sa = s0, sb = min(s0 + 1, n_valid - 1);
+          const float wa = (sa == split) ? 0.f : fast_exp2(__ldcg(p.ws_m + pbase + (int64_t)sa * 256) - m_ref);
+          const float wb = (s0 + 1 >= n_valid || sb == split)
+                               ? 0.f : fast_exp2(__ldcg(p.ws_m + pbase + (int64_t)sb * 256) - m_ref);
+          const float* xa = p.ws_acc + ((int64_t)unit * p.nsplit + sa) * HD * 256 + prow + c * 32 * 256;
+          const float* xb = p.ws_acc + ((int64_t)unit * p.nsplit + sb) * HD * 256 + prow + c * 32 * 256;
+          float va[32], vb[32];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float4 v4 = __ldcg(src + e);
-            orr[4 * e] = __float_as_uint(fmaf(w, v4.x, __uint_as_float(orr[4 * e])));
-            orr[4 * e + 1] = __float_as_uint(fmaf(w, v4.y, __uint_as_float(orr[4 * e + 1])));
-            orr[4 * e + 2] = __float_as_uint(fmaf(w, v4.z, __uint_as_float(orr[4 * e + 2])));
-            orr[4 * e + 3] = __float_as_uint(fmaf(w, v4.w, __uint_as_float(orr[4 * e + 3])));
+          for (int e = 0; e < 32; ++e) {
+            va[e] = __ldcg(xa + e * 256);
+            vb[e] = __ldcg(xb + e * 256);
           }
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            orr[e] = __float_as_uint(fmaf(wb, vb[e], fmaf(wa, va[e], __uint_as_float(orr[e]))));
         }
       }
 #pragma unroll
