@@ -110,6 +110,18 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch. The host launches the prefill and streaming
+// kernels with programmatic stream serialisation, so a grid may start while the
+// previous kernel on the stream is still finishing. Every thread calls pdl_wait()
+// before its first global memory access (read or write): it returns once the
+// previous grid has completed and its writes are visible (at once when there is
+// none). pdl_trigger() lets the next such grid start its prologue on SMs this grid
+// frees; it takes effect when every CTA of this grid has triggered or exited.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+// ---------------------------------------------------------------------------
 // TMA (cp.async.bulk.tensor): plain tile loads and stores of this GPU's own memory.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {

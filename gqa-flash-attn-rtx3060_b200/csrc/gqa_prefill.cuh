@@ -165,6 +165,10 @@ __global__ void __launch_bounds__(384, 1)
     fence_mbar_init();
     fence_proxy_async_smem();
   }
+  // Before any global memory access and before taking TMEM, the previous grid on
+  // the stream has finished (programmatic dependent launch).
+  pdl_wait();
+  pdl_trigger();
   if (warp == 8) {
     tmem_alloc(smem_u32(tmem_base_ptr), Cfg::kTmemCols);
     tmem_relinquish();

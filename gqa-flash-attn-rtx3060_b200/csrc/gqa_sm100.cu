@@ -5,6 +5,7 @@
 // enqueues the kernels on the caller's stream. Nothing here allocates device
 // memory or synchronises (except gqa_device_error, which says so).
 #include <mutex>
+#include <utility>
 #include <vector>
 
 #include "gqa_common.cuh"
@@ -155,6 +156,25 @@ int launch_status() {
   return e == cudaSuccess ? GQA_OK : GQA_ERR_CUDA;
 }
 
+// Launch with programmatic stream serialisation: the kernel may begin while the
+// previous kernel on the stream finishes; it calls pdl_wait() before any global
+// memory access, so stream order holds for every byte it reads or writes.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, int threads, int smem, cudaStream_t st,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 // ----------------------------------------------------------------------------- streaming plan
 // Number of packed rows (group * block_m) the streaming kernel handles per unit.
 constexpr int kStreamMaxRows = 64;
@@ -274,11 +294,10 @@ cudaError_t launch_stream_hd(const StreamParams& p, const StreamPlan& pl, const 
   const dim3 grid(pl.units * pl.nsplit);
   const int smem = StreamCfg<HD>::kSmemBytes;
   switch (pl.rg) {
-    case 1: gqa_stream_kernel<HD, BF, 1><<<grid, StreamCfg<HD>::kThreads, smem, st>>>(p, km, vm); break;
-    case 2: gqa_stream_kernel<HD, BF, 2><<<grid, StreamCfg<HD>::kThreads, smem, st>>>(p, km, vm); break;
-    default: gqa_stream_kernel<HD, BF, 4><<<grid, StreamCfg<HD>::kThreads, smem, st>>>(p, km, vm); break;
+    case 1: return launch_pdl(gqa_stream_kernel<HD, BF, 1>, grid, StreamCfg<HD>::kThreads, smem, st, p, km, vm);
+    case 2: return launch_pdl(gqa_stream_kernel<HD, BF, 2>, grid, StreamCfg<HD>::kThreads, smem, st, p, km, vm);
+    default: return launch_pdl(gqa_stream_kernel<HD, BF, 4>, grid, StreamCfg<HD>::kThreads, smem, st, p, km, vm);
   }
-  return cudaGetLastError();
 }
 
 // Fills the common fields of StreamParams and launches.
@@ -441,8 +460,10 @@ int gqa_fwd(const void* q, const void* k, const void* v, void* o, const int64_t*
   if (grid > 0x7fffffff) return GQA_ERR_INVALID_ARG;
   const bool bf = dtype == GQA_DTYPE_BF16;
   const bool split = p.nsplit > 1;  // the unsplit instantiation carries no split code
+  cudaError_t le = cudaSuccess;
 #define GQA_LAUNCH_PREFILL(HD, BF, SP) \
-  gqa_prefill_kernel<HD, BF, SP><<<(unsigned)grid, PrefillCfg<HD>::kThreads, PrefillCfg<HD>::kSmemBytes, st>>>(p, qm, km, vm, om)
+  le = launch_pdl(gqa_prefill_kernel<HD, BF, SP>, dim3((unsigned)grid), PrefillCfg<HD>::kThreads, \
+             PrefillCfg<HD>::kSmemBytes, st, p, qm, km, vm, om)
   if (head_dim == 128) {
     if (bf) { if (split) GQA_LAUNCH_PREFILL(128, true, true); else GQA_LAUNCH_PREFILL(128, true, false); }
     else { if (split) GQA_LAUNCH_PREFILL(128, false, true); else GQA_LAUNCH_PREFILL(128, false, false); }
@@ -451,6 +472,10 @@ int gqa_fwd(const void* q, const void* k, const void* v, void* o, const int64_t*
     else { if (split) GQA_LAUNCH_PREFILL(64, false, true); else GQA_LAUNCH_PREFILL(64, false, false); }
   }
 #undef GQA_LAUNCH_PREFILL
+  if (le != cudaSuccess) {
+    (void)cudaGetLastError();
+    return GQA_ERR_CUDA;
+  }
   return launch_status();
 }
 

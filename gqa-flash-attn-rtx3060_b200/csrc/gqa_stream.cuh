@@ -158,8 +158,12 @@ __global__ void __launch_bounds__(288, 1)
       tma_prefetch_desc(&kmap);
       tma_prefetch_desc(&vmap);
     }
+    pdl_wait();
     for (int t = 0; t < n_first; ++t) issue(t);
+  } else {
+    pdl_wait();  // before any global access (Q reads, partials, the output)
   }
+  pdl_trigger();
   __syncthreads();
 
   if (warp == NW) {
