@@ -329,16 +329,22 @@ __global__ void __launch_bounds__(288, 1)
 
   // ---- merge the KS warps of each row group through shared memory
   GQA_CBAR();  // every compute warp is done with the ring
+  // acc rows are padded to HD + 8 floats: the 8 row lanes of a float2 store then
+  // start 8 banks apart and each store takes the minimum two wavefronts. Rows of
+  // the upper half of a row group are stored only when the unit has them.
+  constexpr int AS = HD + 8;
   float* mbuf = reinterpret_cast<float*>(smem);  // [NW][16]
   float* lbuf = mbuf + NW * 16;                  // [NW][16]
-  float* abuf = lbuf + NW * 16;                  // [NW][16][HD]
+  float* abuf = lbuf + NW * 16;                  // [NW][16][AS]
+  static_assert((2 * NW * 16 + NW * 16 * AS + 128 + 64 * KS) * 4 <= Cfg::kRingBytes, "merge buffers fit the ring");
   {
-    float* aw = abuf + warp * 16 * HD;
+    float* aw = abuf + warp * 16 * AS;
+    const bool upper = rg * 16 + 8 < p.rows;  // warp-uniform
 #pragma unroll
     for (int i = 0; i < NDB; ++i) {
       const int d = i * 8 + gc * 2;
-      *reinterpret_cast<float2*>(aw + gr * HD + d) = make_float2(acc[i][0], acc[i][1]);
-      *reinterpret_cast<float2*>(aw + (gr + 8) * HD + d) = make_float2(acc[i][2], acc[i][3]);
+      *reinterpret_cast<float2*>(aw + gr * AS + d) = make_float2(acc[i][0], acc[i][1]);
+      if (upper) *reinterpret_cast<float2*>(aw + (gr + 8) * AS + d) = make_float2(acc[i][2], acc[i][3]);
     }
     if (gc == 0) {
       mbuf[warp * 16 + gr] = m_run[0];
@@ -350,7 +356,7 @@ __global__ void __launch_bounds__(288, 1)
   GQA_CBAR();
 
   // Combined per-row (M, L) of this CTA and the per-warp weights.
-  float* fin_m = abuf + NW * 16 * HD;  // [64]
+  float* fin_m = abuf + NW * 16 * AS;  // [64]
   float* fin_l = fin_m + 64;           // [64]
   float* fin_w = fin_l + 64;           // [64][KS]
   if (tid < RG * 16) {
@@ -380,7 +386,7 @@ __global__ void __launch_bounds__(288, 1)
 #pragma unroll
     for (int k2 = 0; k2 < KS; ++k2) {
       const float wt = fin_w[r * KS + k2];
-      const float4 v = *reinterpret_cast<const float4*>(abuf + ((k2 * RG + g_rg) * 16 + rr) * HD + d);
+      const float4 v = *reinterpret_cast<const float4*>(abuf + ((k2 * RG + g_rg) * 16 + rr) * AS + d);
       a.x += wt * v.x;
       a.y += wt * v.y;
       a.z += wt * v.z;
