@@ -17,7 +17,9 @@ replayed back to back from CUDA graphs of up to 16 steps cycling 4 input copies
 (268 MB > L2), the K timed steps between one pair of events. `value` is
 algorithmic FLOPs (causal pairs only) or algorithmic bytes of all ranks /
 max-over-ranks time. `e2e` repeats the metric through the public API with
-pinned host inputs copied in and the output copied back inside the timed region.
+pinned host inputs copied in and the output copied back inside the timed region,
+double-buffered as a serving loop does (the next step's inputs copy in while a
+step computes).
 
 --impl reference times the reference's CPU path (the numpy port of
 tests/reference.py in oracle/) on the host cores on a bounded sample of the
@@ -354,36 +356,65 @@ def run_attention_workload(wl, world, rank, device, steps, warmup, args):
 
 
 def run_e2e(wl, world, rank, device, steps, args):
-    """Same metric through the public API with pinned host buffers: H2D of q/k/v,
-    gqa_flash_attn, D2H of o, all inside the timed region."""
+    """Same metric through the public API with pinned host buffers, as a serving loop
+    runs it: every step copies its own q/k/v in (H2D), calls gqa_flash_attn and copies
+    o back (D2H). Inputs are double-buffered: step i+1's H2D runs on a copy stream
+    while step i computes, and step i's D2H on a third stream (PCIe is full duplex).
+    The K timed steps sit between one pair of events (barrier and synchronize on both
+    sides), all copies included."""
     from gqa_kernels import gqa_flash_attn
     B, Hq, Hkv, Sq, Skv, D = wl["B"], wl["Hq"], wl["Hkv"], wl["Sq"], wl["Skv"], wl["D"]
     if args.workload not in ("prefill", "decode"):
         return None
     g = torch.Generator().manual_seed(rank)
-    qh = torch.randn(B, Hq, Sq, D, generator=g).to(torch.bfloat16).pin_memory()
-    kh = torch.randn(B, Hkv, Skv, D, generator=g).to(torch.bfloat16).pin_memory()
-    vh = torch.randn(B, Hkv, Skv, D, generator=g).to(torch.bfloat16).pin_memory()
-    oh = torch.empty(B, Hq, Sq, D, dtype=torch.bfloat16).pin_memory()
-    qd, kd, vd = (torch.empty(t.shape, dtype=t.dtype, device=device) for t in (qh, kh, vh))
 
-    def step(i):
-        qd.copy_(qh, non_blocking=True)
-        kd.copy_(kh, non_blocking=True)
-        vd.copy_(vh, non_blocking=True)
-        o = gqa_flash_attn(qd, kd, vd, causal=True)
-        oh.copy_(o, non_blocking=True)
-    times, _ = timed_steps(step, steps, 2, world, device)
+    def host(*shape):
+        return torch.randn(*shape, generator=g).to(torch.bfloat16).pin_memory()
+    hosts = [(host(B, Hq, Sq, D), host(B, Hkv, Skv, D), host(B, Hkv, Skv, D)) for _ in range(2)]
+    outs = [torch.empty(B, Hq, Sq, D, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    dev = [tuple(torch.empty(t.shape, dtype=t.dtype, device=device) for t in hs) for hs in hosts]
+    comp = torch.cuda.current_stream(device)
+    s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    ev_in = [torch.cuda.Event() for _ in range(2)]    # inputs of buffer b landed
+    ev_done = [torch.cuda.Event() for _ in range(2)]  # the step on buffer b finished computing
+
+    def h2d(i):
+        b = i % 2
+        s_in.wait_event(ev_done[b])  # the step two back has finished reading buffer b
+        with torch.cuda.stream(s_in):
+            for d, h in zip(dev[b], hosts[b]):
+                d.copy_(h, non_blocking=True)
+        ev_in[b].record(s_in)
+
+    def run_steps(n):
+        if n <= 0:
+            return
+        h2d(0)
+        for i in range(n):
+            if i + 1 < n:
+                h2d(i + 1)
+            b = i % 2
+            comp.wait_event(ev_in[b])
+            o = gqa_flash_attn(*dev[b], causal=True)
+            ev_done[b].record(comp)
+            s_out.wait_event(ev_done[b])
+            with torch.cuda.stream(s_out):
+                outs[b].copy_(o, non_blocking=True)
+            o.record_stream(s_out)
+        comp.wait_stream(s_out)
+
+    times, _ = timed_loop(run_steps, steps, 3, world, device)
     ms = max_over_ranks(sum(times), world, device) / steps
     mult = world if wl["scaling"] == "weak" else 1
-    h2d = sum(t.numel() * t.element_size() for t in (qh, kh, vh))
-    d2h = oh.numel() * oh.element_size()
+    h2d_bytes = sum(t.numel() * t.element_size() for t in hosts[0])
+    d2h_bytes = outs[0].numel() * outs[0].element_size()
     if wl["bound"] == "tensor":
         val, unit = attn_flops(B, Hq, Sq, Skv, D) * mult / (ms * 1e-3) / 1e12, "TFLOP/s"
     else:
         val, unit = attn_bytes(B, Hq, Hkv, Sq, Skv, D) * mult / (ms * 1e-3) / 1e9, "GB/s"
     return {"value": round(val, 3), "unit": unit, "ms_per_step": round(ms, 4),
-            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+            "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes,
+            "pipeline": "inputs double-buffered: H2D of step i+1 and D2H of step i overlap step i"}
 
 
 # ----------------------------------------------------------------------------- CPU baseline (oracle)
