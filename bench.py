@@ -1,6 +1,6 @@
 """Benchmark of the B200 GQA flash-attention forward (driver contract).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|sdpa|flash_attn]
                     [--workload prefill|decode|chunked|long_decode]
 
 Default workload (BASELINE metric "prefill TFLOP/s @8K causal; decode HBM GB/s
@@ -23,7 +23,10 @@ step computes).
 
 --impl reference times the reference's CPU path (the numpy port of
 tests/reference.py in oracle/) on the host cores on a bounded sample of the
-same workload; under torchrun only rank 0 runs it.
+same workload; under torchrun only rank 0 runs it. --impl sdpa and --impl
+flash_attn time same-box library comparators (torch SDPA, flash_attn 2) on the
+same workloads and timing, the role the reference's benchmark/run.py gives
+SDPA and FA2; their lines carry "impl" and report no launches of this library.
 """
 import argparse
 import datetime
@@ -245,10 +248,43 @@ def make_flush(device):
     return flush
 
 
+# ----------------------------------------------------------------------------- attention arms
+def make_attention(impl):
+    """The attention call a step makes: this library (`ours`) or a same-box library
+    comparator (`sdpa`: torch scaled_dot_product_attention; `flash_attn`: flash_attn's
+    flash_attn_func), all with the reference's bottom-right causal rule."""
+    if impl == "ours":
+        from gqa_kernels import gqa_flash_attn
+        return lambda q, k, v: gqa_flash_attn(q, k, v, causal=True)
+    if impl == "sdpa":
+        import torch.nn.functional as F
+        masks = {}
+
+        def sdpa(q, k, v):
+            sq, skv = q.shape[2], k.shape[2]
+            if sq == skv:
+                return F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
+            if sq == 1:  # the one query sees every key
+                return F.scaled_dot_product_attention(q, k, v, enable_gqa=True)
+            key = (sq, skv, q.device)
+            if key not in masks:  # is_causal is top-left aligned: pass the bottom-right mask
+                qpos = torch.arange(sq, device=q.device)[:, None] + (skv - sq)
+                masks[key] = qpos >= torch.arange(skv, device=q.device)[None, :]
+            return F.scaled_dot_product_attention(q, k, v, attn_mask=masks[key], enable_gqa=True)
+        return sdpa
+    if impl == "flash_attn":
+        from flash_attn import flash_attn_func  # bottom-right causal, GQA by head count
+
+        def fa(q, k, v):
+            return flash_attn_func(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), causal=True).transpose(1, 2)
+        return fa
+    raise SystemExit(f"unknown impl {impl}")
+
+
 # ----------------------------------------------------------------------------- our arm
 def run_attention_workload(wl, world, rank, device, steps, warmup, args):
-    from gqa_kernels import gqa_flash_attn
     from gqa_kernels import sharded as S
+    attn = make_attention(args.impl)
     B, Hq, Hkv, Sq, Skv, D = wl["B"], wl["Hq"], wl["Hkv"], wl["Sq"], wl["Skv"], wl["D"]
     dt = torch.bfloat16
     gen = torch.Generator(device=device).manual_seed(rank)
@@ -264,7 +300,7 @@ def run_attention_workload(wl, world, rank, device, steps, warmup, args):
         local["q"], local["k"], local["v"] = rnd(B, Hq, Sq, D), rnd(B, Hkv, Skv, D), rnd(B, Hkv, Skv, D)
 
         def step(i):
-            local["o"] = gqa_flash_attn(local["q"], local["k"], local["v"], causal=True)
+            local["o"] = attn(local["q"], local["k"], local["v"])
         flush = make_flush(device)
         launches_per_step = 1
     elif name == "decode":
@@ -278,7 +314,7 @@ def run_attention_workload(wl, world, rank, device, steps, warmup, args):
         gs.wait_stream(torch.cuda.current_stream(device))
         with torch.cuda.stream(gs):
             for q, k, v in sets:
-                gqa_flash_attn(q, k, v, causal=True)
+                attn(q, k, v)
         gs.synchronize()
         graphs = {}
 
@@ -288,7 +324,7 @@ def run_attention_workload(wl, world, rank, device, steps, warmup, args):
                 with torch.cuda.stream(gs), torch.cuda.graph(g, stream=gs):
                     for i in range(n):
                         q, k, v = sets[i % len(sets)]
-                        local["o"] = gqa_flash_attn(q, k, v, causal=True)
+                        local["o"] = attn(q, k, v)
                 graphs[n] = g
             return graphs[n]
         local["q"], local["k"], local["v"] = sets[0]
@@ -307,7 +343,7 @@ def run_attention_workload(wl, world, rank, device, steps, warmup, args):
         q, k, v = rnd(nb, nh * g, Sq, D), rnd(nb, nh, Skv, D), rnd(nb, nh, Skv, D)
 
         def step(i):
-            local["o"] = S.head_sharded_forward(q, k, v)
+            local["o"] = S.head_sharded_forward(q, k, v) if args.impl == "ours" else attn(q, k, v)
         flush = make_flush(device)
         launches_per_step = 1
     elif name == "long_decode":
@@ -316,8 +352,10 @@ def run_attention_workload(wl, world, rank, device, steps, warmup, args):
         k, v = rnd(B, Hkv, k1 - k0, D), rnd(B, Hkv, k1 - k0, D)
         if world == 1:
             def step(i):
-                local["o"] = gqa_flash_attn(q, k, v, causal=True)
+                local["o"] = attn(q, k, v)
             launches_per_step = 1
+        elif args.impl != "ours":
+            raise SystemExit("the library comparators run the seq_kv-sharded workload on one GPU only")
         else:
             packed = torch.empty(S.packed_size(q.shape), dtype=torch.float32, device=device)
             gathered = torch.empty((world, packed.numel()), dtype=torch.float32, device=device)
@@ -473,7 +511,8 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "sdpa", "flash_attn"], default="ours",
+                    help="reference: the reference's CPU path; sdpa / flash_attn: same-box library comparators")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="prefill")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -489,6 +528,15 @@ def main():
     if args.impl == "reference":
         return main_reference(args, wl, steps)
 
+    comparator = args.impl in ("sdpa", "flash_attn")
+    if comparator:
+        try:
+            make_attention(args.impl)
+        except Exception as e:  # the comparator library is absent or cannot load here
+            if int(os.environ.get("RANK", "0")) == 0:
+                print(json.dumps({"impl": args.impl, "unavailable": f"{type(e).__name__}: {e}"[:300]}), flush=True)
+            return
+        args.no_e2e = args.no_cpu = True
     world, rank, local = dist_setup(args.gpus)
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
@@ -520,7 +568,7 @@ def main():
                    "parallelism": (f"batch-sharded x{world}" if wl["scaling"] == "weak" else
                                    f"kv-head/batch x{world}" if args.workload == "chunked" else
                                    f"seq_kv x{world} + NCCL all-gather LSE combine")},
-        "gpu_launches": res["launches"],
+        "gpu_launches": 0 if comparator else res["launches"],
     }
     # roofline of the dominant kernel, from rank 0's mean per-launch event time. Per-rank
     # work: one workload instance (weak scaling) or 1/world of it (strong scaling).
@@ -561,7 +609,7 @@ def main():
                                            "frac": round(dbytes / (dl_ms * 1e-3) / 1e9 / peaks["hbm"], 4),
                                            "traffic": profile_traffic("decode")},
                               "clocks": dres["clocks"]}
-        line["gpu_launches"] += dres["launches"]
+        line["gpu_launches"] += 0 if comparator else dres["launches"]
 
     if not args.no_e2e:
         e2e = run_e2e(wl, world, rank, device, 20 if args.workload == "prefill" else 200, args)
@@ -576,6 +624,8 @@ def main():
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
+    if comparator:
+        line["impl"] = args.impl  # library kernels on the same box: context, not this library
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
