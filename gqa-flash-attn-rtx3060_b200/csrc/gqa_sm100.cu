@@ -300,13 +300,26 @@ cudaError_t launch_stream_hd(const StreamParams& p, const StreamPlan& pl, const 
   }
 }
 
-// Fills the common fields of StreamParams and launches.
+// Fills the common fields of StreamParams and launches. With `paged`, k/v are paged
+// caches (num_blocks, block_size, hkv, D) and their maps are (D, hkv, block_size,
+// num_blocks) with {64, 1, 64, 1} boxes: the same 64-key x 128-byte smem tiles.
+struct PagedCache {
+  int block_size, num_blocks;
+};
+
 int run_stream(const Shape& s, const StreamPlan& pl, StreamParams p, const void* k, const void* v,
-               const int64_t* ks, const int64_t* vs, int dtype, cudaStream_t st) {
+               const int64_t* ks, const int64_t* vs, int dtype, cudaStream_t st, const PagedCache* paged = nullptr) {
   CUtensorMap km, vm;
-  int rc = make_map(&km, k, ks, s.batch, s.hkv, s.seq_kv, s.head_dim, 64, 1);
-  if (rc) return rc;
-  rc = make_map(&vm, v, vs, s.batch, s.hkv, s.seq_kv, s.head_dim, 64, 1);
+  int rc;
+  if (paged) {
+    const int64_t cs[4] = {(int64_t)paged->block_size * s.hkv * s.head_dim, (int64_t)s.hkv * s.head_dim,
+                           s.head_dim, 1};
+    rc = make_map(&km, k, cs, paged->num_blocks, paged->block_size, s.hkv, s.head_dim, 1, 64);
+    if (!rc) rc = make_map(&vm, v, cs, paged->num_blocks, paged->block_size, s.hkv, s.head_dim, 1, 64);
+  } else {
+    rc = make_map(&km, k, ks, s.batch, s.hkv, s.seq_kv, s.head_dim, 64, 1);
+    if (!rc) rc = make_map(&vm, v, vs, s.batch, s.hkv, s.seq_kv, s.head_dim, 64, 1);
+  }
   if (rc) return rc;
   p.batch = s.batch;
   p.hq = s.hq;
@@ -376,6 +389,70 @@ int gqa_version(void) { return 100; }
 int gqa_sm_count(void) {
   int sm = 0;
   return current_device(&sm) == GQA_OK ? sm : 0;
+}
+
+size_t gqa_paged_decode_workspace_bytes(int num_seqs, int num_heads, int num_kv_heads, int max_seq_len,
+                                        int head_dim) {
+  Shape s;
+  if (check_shape(num_seqs, num_heads, num_kv_heads, 1, max_seq_len, head_dim, &s)) return 0;
+  if (num_seqs == 0 || max_seq_len == 0 || s.group > kStreamMaxRows) return 0;
+  int sm = 0;
+  if (current_device(&sm)) return 0;
+  const StreamPlan pl = plan_stream(s, sm, true);
+  return pl.nsplit > 1 ? stream_ws_bytes(pl, head_dim) : 0;
+}
+
+int gqa_paged_decode(const void* q, const void* k_cache, const void* v_cache, void* o, const int64_t* qs3,
+                     const int64_t* os3, const int* block_table, int bt_stride, const int* seq_lens, int num_seqs,
+                     int num_heads, int num_kv_heads, int head_dim, int block_size, int num_blocks, int max_seq_len,
+                     float scale_log2, int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  Shape s;
+  int rc = check_shape(num_seqs, num_heads, num_kv_heads, 1, max_seq_len, head_dim, &s);
+  if (rc) return rc;
+  if (!qs3 || !os3) return GQA_ERR_INVALID_ARG;
+  if (num_seqs == 0) return GQA_OK;
+  if (dtype != GQA_DTYPE_BF16 && dtype != GQA_DTYPE_F16) return GQA_ERR_UNSUPPORTED;
+  if (s.group > kStreamMaxRows) return GQA_ERR_UNSUPPORTED;  // the group's heads fill one streaming unit
+  if (block_size < 64 || (block_size & (block_size - 1)) != 0 || num_blocks <= 0) return GQA_ERR_UNSUPPORTED;
+  if (!k_cache || !v_cache || !block_table || !seq_lens || bt_stride <= 0) return GQA_ERR_INVALID_ARG;
+  if (max_seq_len > (int64_t)bt_stride * block_size) return GQA_ERR_INVALID_ARG;
+  if (!aligned16(k_cache) || !aligned16(v_cache)) return GQA_ERR_ALIGNMENT;
+  const int64_t qs[4] = {qs3[0], qs3[1], 0, qs3[2]};  // (b, h, s, d), one query position
+  const int64_t os[4] = {os3[0], os3[1], 0, os3[2]};
+  rc = check_strides(q, qs);
+  if (!rc) rc = check_strides(o, os);
+  if (rc) return rc;
+  int sm = 0;
+  rc = current_device(&sm);
+  if (rc) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (max_seq_len == 0) return fill_nan(o, os, s, dtype, st);
+
+  StreamPlan pl = plan_stream(s, sm, true);
+  StreamParams p{};
+  p.q = reinterpret_cast<const uint16_t*>(q);
+  p.o = o;
+  p.q_sb = qs[0]; p.q_sh = qs[1]; p.q_sm = 0;
+  p.o_sb = os[0]; p.o_sh = os[1]; p.o_sm = 0;
+  p.causal = 0;  // the one new token of each sequence sees all its cached keys
+  p.scale_log2 = scale_log2;
+  p.kv_offset = 0;
+  p.seq_kv_total = max_seq_len;
+  p.block_table = block_table;
+  p.seq_lens = seq_lens;
+  p.bt_stride = bt_stride;
+  int shift = 0;
+  while ((1 << shift) < block_size) ++shift;
+  p.block_shift = shift;
+  if (pl.nsplit > 1 && workspace && workspace_bytes >= stream_ws_bytes(pl, head_dim)) {
+    p.mode = kStreamFused;
+    stream_ws_carve(pl, head_dim, workspace, &p);
+  } else {
+    pl = plan_stream(s, sm, false);
+    p.mode = kStreamOut;
+  }
+  const PagedCache pc{block_size, num_blocks};
+  return run_stream(s, pl, p, k_cache, v_cache, nullptr, nullptr, dtype, st, &pc);
 }
 
 size_t gqa_fwd_workspace_bytes(int batch, int num_heads, int num_kv_heads, int seq_q, int seq_kv, int head_dim) {

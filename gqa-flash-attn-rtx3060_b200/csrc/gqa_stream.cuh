@@ -56,6 +56,15 @@ struct StreamParams {
   float* m_out;
   float* l_out;
   float* acc_out;
+  // Paged K/V (block_table != nullptr): the caches are [num_blocks][block_size][hkv][HD]
+  // (the K/V tensor maps are (HD, hkv, block_size, num_blocks)); sequence b's key k lives
+  // in physical block block_table[b * bt_stride + (k >> block_shift)] at position
+  // k & (block_size - 1), and the sequence holds seq_lens[b] keys. block_size is a power
+  // of two >= 64, so a 64-key box never crosses a block.
+  const int* block_table;
+  const int* seq_lens;
+  int bt_stride;
+  int block_shift;
 };
 
 template <int HD>
@@ -113,38 +122,12 @@ __global__ void __launch_bounds__(288, 1)
   const int kvh = (unit / p.n_mtiles) % p.hkv;
   const int b = unit / (p.n_mtiles * p.hkv);
   const int off = p.seq_kv_total - p.seq_q;  // bottom-right causal offset (global)
+  const bool paged = p.block_table != nullptr;
 
-  // Highest key (local, exclusive) any valid row of this unit may see.
-  int kv_end = p.seq_kv;
-  if (p.causal) {
-    const int last_pos = min((mt + 1) * p.block_m, p.seq_q) - 1;
-    kv_end = min(kv_end, last_pos + off - p.kv_offset + 1);
-  }
-  const int k_begin = split * p.chunk;
-  const int k_end = min(k_begin + p.chunk, kv_end);
-  const int n_stages = (k_end > k_begin) ? (k_end - k_begin + Cfg::kBN - 1) / Cfg::kBN : 0;
-
-  // The producer thread initialises the barriers and issues the first ring of
-  // loads before the CTA-wide barrier, so HBM requests start at once. A stage
-  // holds one or two 64-key boxes of K and of V (the chunk's last stage may be half).
-  auto issue = [&](int t) {
-    const int slot = t % Cfg::kStages;
-    const uint32_t full = bar_full + 8 * slot;
-    const int key0 = k_begin + t * Cfg::kBN;
-    const int halves = (min(Cfg::kBN, k_end - key0) + Cfg::kBox - 1) / Cfg::kBox;
-    mbar_arrive_expect_tx(full, halves * 2 * Cfg::kNSub * Cfg::kBoxBytes);
-    const uint32_t kdst = base + slot * Cfg::kStageBytes;
-    const uint32_t vdst = kdst + Cfg::kTileBytes;
-    for (int h = 0; h < halves; ++h) {
-#pragma unroll
-      for (int s = 0; s < Cfg::kNSub; ++s) {
-        const uint32_t o = s * Cfg::kSubBytes + h * Cfg::kBoxBytes;
-        tma_load_4d(kdst + o, &kmap, full, s * 64, key0 + h * Cfg::kBox, kvh, b);
-        tma_load_4d(vdst + o, &vmap, full, s * 64, key0 + h * Cfg::kBox, kvh, b);
-      }
-    }
-  };
-  const int n_first = min(n_stages, Cfg::kStages);
+  // The producer thread initialises the barriers; every thread then waits for the
+  // previous grid on the stream before its first global access (the sequence length
+  // of a paged call included), and the producer issues the first ring of loads
+  // before the CTA-wide barrier, so HBM requests start at once.
   if (tid == CT) {
     for (int s = 0; s < Cfg::kStages; ++s) {
       mbar_init(bar_full + 8 * s, 1);
@@ -154,14 +137,64 @@ __global__ void __launch_bounds__(288, 1)
     *abort_flag = 0;
     fence_mbar_init();
     fence_proxy_async_smem();
-    if (n_stages > 0) {
-      tma_prefetch_desc(&kmap);
-      tma_prefetch_desc(&vmap);
+    tma_prefetch_desc(&kmap);
+    tma_prefetch_desc(&vmap);
+  }
+  pdl_wait();
+
+  // Highest key (local, exclusive) any valid row of this unit may see.
+  int kv_end = p.seq_kv;
+  if (paged) kv_end = min(kv_end, p.seq_lens[b]);
+  if (p.causal) {
+    const int last_pos = min((mt + 1) * p.block_m, p.seq_q) - 1;
+    kv_end = min(kv_end, last_pos + off - p.kv_offset + 1);
+  }
+  const int k_begin = split * p.chunk;
+  const int k_end = min(k_begin + p.chunk, kv_end);
+  const int n_stages = (k_end > k_begin) ? (k_end - k_begin + Cfg::kBN - 1) / Cfg::kBN : 0;
+
+  // A stage holds one or two 64-key boxes of K and of V (the chunk's last stage may
+  // be half). Paged calls look up the physical block of each box; the producer loads
+  // those indices before it waits for the stage's slot, so the lookup overlaps the wait.
+  auto stage_blocks = [&](int t, int& pb0, int& pb1) {
+    pb0 = pb1 = 0;
+    if (!paged) return;
+    const int key0 = k_begin + t * Cfg::kBN;
+    const int* row_bt = p.block_table + (int64_t)b * p.bt_stride;
+    pb0 = row_bt[key0 >> p.block_shift];
+    if (key0 + Cfg::kBox < k_end) pb1 = row_bt[(key0 + Cfg::kBox) >> p.block_shift];
+  };
+  auto issue = [&](int t, int pb0, int pb1) {
+    const int slot = t % Cfg::kStages;
+    const uint32_t full = bar_full + 8 * slot;
+    const int key0 = k_begin + t * Cfg::kBN;
+    const int halves = (min(Cfg::kBN, k_end - key0) + Cfg::kBox - 1) / Cfg::kBox;
+    mbar_arrive_expect_tx(full, halves * 2 * Cfg::kNSub * Cfg::kBoxBytes);
+    const uint32_t kdst = base + slot * Cfg::kStageBytes;
+    const uint32_t vdst = kdst + Cfg::kTileBytes;
+    for (int h = 0; h < halves; ++h) {
+      const int key = key0 + h * Cfg::kBox;
+      // dense: (d, key, head, batch); paged: (d, head, position in block, physical block)
+      const int c1 = paged ? kvh : key;
+      const int c2 = paged ? (key & ((1 << p.block_shift) - 1)) : kvh;
+      const int c3 = paged ? (h ? pb1 : pb0) : b;
+#pragma unroll
+      for (int s = 0; s < Cfg::kNSub; ++s) {
+        const uint32_t o = s * Cfg::kSubBytes + h * Cfg::kBoxBytes;
+        tma_load_4d(kdst + o, &kmap, full, s * 64, c1, c2, c3);
+        tma_load_4d(vdst + o, &vmap, full, s * 64, c1, c2, c3);
+      }
     }
-    pdl_wait();
-    for (int t = 0; t < n_first; ++t) issue(t);
-  } else {
-    pdl_wait();  // before any global access (Q reads, partials, the output)
+  };
+  const int n_first = min(n_stages, Cfg::kStages);
+  if (tid == CT) {
+    int pb[Cfg::kStages][2];
+#pragma unroll
+    for (int t = 0; t < Cfg::kStages; ++t)
+      if (t < n_first) stage_blocks(t, pb[t][0], pb[t][1]);
+#pragma unroll
+    for (int t = 0; t < Cfg::kStages; ++t)
+      if (t < n_first) issue(t, pb[t][0], pb[t][1]);
   }
   pdl_trigger();
   __syncthreads();
@@ -172,8 +205,10 @@ __global__ void __launch_bounds__(288, 1)
       int t = n_first;
       for (; t < n_stages; ++t) {
         const int slot = t % Cfg::kStages;
+        int pb0, pb1;
+        stage_blocks(t, pb0, pb1);
         if (!mbar_wait(bar_empty + 8 * slot, (t / Cfg::kStages - 1) & 1, abort_flag, 101)) break;
-        issue(t);
+        issue(t, pb0, pb1);
       }
       // On abort, let the loads already issued land before the CTA exits.
       if (t < n_stages) {

@@ -42,6 +42,9 @@ SIGNATURES = {
                          _P, _SZ, _P]),
     "gqa_lse_combine": (_I, [_P, _P, _P, _I, ctypes.c_int64, ctypes.c_int64, _P, _I64P, _I, _I, _I, _I, _I, _P]),
     "gqa_device_error": (_I, [ctypes.POINTER(_I), ctypes.POINTER(_I), _I]),
+    "gqa_paged_decode_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),
+    "gqa_paged_decode": (_I, [_P, _P, _P, _P, _I64P, _I64P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P,
+                              _SZ, _P]),
 }
 
 _lib = None

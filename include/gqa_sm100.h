@@ -161,6 +161,30 @@ int gqa_lse_combine(const float* m_parts, const float* l_parts, const float* acc
                     int num_heads, int seq_q, int head_dim, int dtype, void* stream);
 
 /*
+ * Paged decode: one new query token per sequence attends to that sequence's
+ * cached keys, read from a paged K/V cache in the layout vLLM uses,
+ * k_cache/v_cache (num_blocks, block_size, num_kv_heads, head_dim), contiguous.
+ * Sequence b holds seq_lens[b] keys; its key k lives in physical block
+ * block_table[b * bt_stride + k / block_size] at position k % block_size.
+ * q/o are (num_seqs, num_heads, head_dim) with element strides q_strides3 /
+ * o_strides3 (seq, head, d; d stride 1). block_size must be a power of two
+ * >= 64; block_table and seq_lens are int32 device arrays; max_seq_len bounds
+ * every seq_lens[b] and sizes the key split (the workspace query takes it).
+ * A sequence with no key gives NaN, as the dense path does. The split
+ * combine is fused into the launch when the workspace (zeroed before first
+ * use; every call leaves it zero) holds gqa_paged_decode_workspace_bytes().
+ * No reference counterpart: the reference's roadmap names a vLLM-shaped
+ * interface (README.md:144); the attention is gqa_kernels/gqa_split.py's.
+ */
+size_t gqa_paged_decode_workspace_bytes(int num_seqs, int num_heads, int num_kv_heads, int max_seq_len,
+                                        int head_dim);
+int gqa_paged_decode(const void* q, const void* k_cache, const void* v_cache, void* o, const int64_t* q_strides3,
+                     const int64_t* o_strides3, const int* block_table, int bt_stride, const int* seq_lens,
+                     int num_seqs, int num_heads, int num_kv_heads, int head_dim, int block_size, int num_blocks,
+                     int max_seq_len, float scale_log2, int dtype, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/*
  * Reads (and clears, if `clear` is nonzero) the device error word of the
  * current device: 0, or GQA_ERR_TIMEOUT when a bounded in-kernel wait expired.
  * `site` (optional) receives the wait site id. Synchronises the current device.
