@@ -102,12 +102,10 @@ struct PrefillCfg {
   static constexpr int kControlRegs = 88;
   static constexpr int kRegsNeeded = 256 * kSoftmaxRegs + 128 * kControlRegs;  // 64512 = 384 x 168
   static constexpr int kColS0 = 0, kColS1 = 128, kColO0 = 256, kColO1 = 256 + HD;
-  // Of every four column pairs of P, this many take the MUFU ex2 and the rest the
-  // polynomial exp2 on the FMA pipe (exp2_poly2): the split that balances the two pipes.
-#ifndef GQA_PREFILL_MUFU_PAIRS_PER4
-#define GQA_PREFILL_MUFU_PAIRS_PER4 3
-#endif
-  static constexpr int kMufuPairsPer4 = GQA_PREFILL_MUFU_PAIRS_PER4;
+  // Of every eight column pairs of P, this many take the MUFU ex2 and the rest the
+  // polynomial exp2 on the FMA pipe (exp2_poly2). Measured on B200 (8K causal
+  // prefill): 7 of 8 472 us, 8 of 8 473 us, 6 of 8 490 us, 5 of 8 514 us.
+  static constexpr int kMufuPairsPer8 = 7;
 };
 
 template <int HD, bool BF16, bool SPLIT>
@@ -393,7 +391,7 @@ __global__ void __launch_bounds__(384, 1)
       }
       // P = exp2(S * scale - m), written over S as packed 16-bit pairs, in two 64-key
       // halves so the PV MMAs of the first half start while the second is computed.
-      // One column pair in four takes the polynomial exp2 on the FMA pipe, the rest
+      // One column pair in eight takes the polynomial exp2 on the FMA pipe, the rest
       // the MUFU ex2; the row sum and the scale use packed two-lane fp32 math.
       const float2 sc2 = make_float2(scale, scale);
       const float2 nm2 = make_float2(-m_run, -m_run);
@@ -406,7 +404,7 @@ __global__ void __launch_bounds__(384, 1)
           const int col = 64 * h + 2 * c;
           const float2 x = fma2(make_float2(__uint_as_float(sr[col]), __uint_as_float(sr[col + 1])), sc2, nm2);
           float2 pv;
-          if ((c & 3) >= Cfg::kMufuPairsPer4) {
+          if ((c & 7) >= Cfg::kMufuPairsPer8) {
             pv = exp2_poly2(x);
           } else {
             pv.x = fast_exp2(x.x);
