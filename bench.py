@@ -443,6 +443,19 @@ def run_e2e(wl, world, rank, device, steps, args):
 
     times, _ = timed_loop(run_steps, steps, 3, world, device)
     ms = max_over_ranks(sum(times), world, device) / steps
+    # This box's pinned host<->device bandwidth (outside the timed region): the e2e
+    # number is bound by it, and PCIe links differ between machines of a pool.
+    link = {}
+    for name, dst, src in (("h2d_gbs", dev[0][1], hosts[0][1]), ("d2h_gbs", outs[0], dev[0][0])):
+        dst.copy_(src, non_blocking=True)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(device)
+        a.record(comp)
+        for _ in range(5):
+            dst.copy_(src, non_blocking=True)
+        b.record(comp)
+        torch.cuda.synchronize(device)
+        link[name] = round(5 * src.numel() * src.element_size() / (a.elapsed_time(b) * 1e-3) / 1e9, 1)
     mult = world if wl["scaling"] == "weak" else 1
     h2d_bytes = sum(t.numel() * t.element_size() for t in hosts[0])
     d2h_bytes = outs[0].numel() * outs[0].element_size()
@@ -452,7 +465,8 @@ def run_e2e(wl, world, rank, device, steps, args):
         val, unit = attn_bytes(B, Hq, Hkv, Sq, Skv, D) * mult / (ms * 1e-3) / 1e9, "GB/s"
     return {"value": round(val, 3), "unit": unit, "ms_per_step": round(ms, 4),
             "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes,
-            "pipeline": "inputs double-buffered: H2D of step i+1 and D2H of step i overlap step i"}
+            "pipeline": "inputs double-buffered: H2D of step i+1 and D2H of step i overlap step i",
+            "link": link}
 
 
 # ----------------------------------------------------------------------------- CPU baseline (oracle)
