@@ -4,7 +4,6 @@ Physical blocks are shuffled across sequences; lengths cover 0, 1, block edges a
 long sequences that take the fused key split."""
 import ctypes
 
-import numpy as np
 import pytest
 import torch
 
@@ -46,11 +45,12 @@ def _dense(kc, bt_row, s, block_size):
     return torch.cat(blocks, dim=0)[:s].permute(1, 0, 2).unsqueeze(0)
 
 
-@pytest.mark.parametrize("block_size,D", [(64, 128), (128, 128), (256, 64)])
-def test_paged_decode_matches_dense_reference(block_size, D):
+@pytest.mark.parametrize("block_size,D,dtype", [(64, 128, torch.bfloat16), (128, 128, torch.float16),
+                                                (256, 64, torch.bfloat16)])
+def test_paged_decode_matches_dense_reference(block_size, D, dtype):
     seq_lens = [1, 63, 64, 65, 1000, 4097, 17000]
     Hq, Hkv = 32, 8
-    q, kc, vc, bt, sl = _paged_case(seq_lens, Hq, Hkv, D, block_size, seed=block_size + D)
+    q, kc, vc, bt, sl = _paged_case(seq_lens, Hq, Hkv, D, block_size, seed=block_size + D, dtype=dtype)
     out = paged_decode(q, kc, vc, bt, sl)
     torch.cuda.synchronize()
     btc = bt.cpu()
