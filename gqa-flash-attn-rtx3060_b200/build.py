@@ -1,6 +1,6 @@
 """Builds libgqa_sm100.so (the C-ABI library) in-tree for sm_100a.
 
-    python gqa-flash-attn-rtx3060_b200/build.py [--force]
+    python gqa-flash-attn-rtx3060_b200/build.py [--force] [--debug]
 
 The library is one translation unit (csrc/gqa_sm100.cu) compiled by nvcc with
 `-gencode arch=compute_100a,code=sm_100a` and the static CUDA runtime; it does
@@ -17,6 +17,10 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 OUT = os.path.join(HERE, "gqa_kernels", "libgqa_sm100.so")
+# Debug variant: in-kernel address/coordinate checks (GQA_DEBUG_CHECKS) that report
+# GQA_ERR_DEBUG_CHECK instead of faulting; selected at run time with
+# GQA_KERNELS_LIB=debug.
+OUT_DEBUG = os.path.join(HERE, "gqa_kernels", "libgqa_sm100_debug.so")
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -33,10 +37,10 @@ def _sources():
     )
 
 
-def up_to_date():
-    if not os.path.exists(OUT):
+def up_to_date(out=OUT):
+    if not os.path.exists(out):
         return False
-    t = os.path.getmtime(OUT)
+    t = os.path.getmtime(out)
     return all(os.path.getmtime(s) <= t for s in _sources())
 
 
@@ -47,24 +51,28 @@ def nvcc():
     return path
 
 
-def build(force=False, verbose=False):
-    """Compiles the library unless it is newer than every source. Returns its path."""
-    if not force and up_to_date():
-        return OUT
-    tmp = OUT + ".tmp"
-    cmd = [nvcc(), *NVCC_FLAGS, "-I", INCLUDE, "-o", tmp, os.path.join(CSRC, "gqa_sm100.cu")]
+def build(force=False, verbose=False, debug=False):
+    """Compiles the library (or, with debug, its checked variant) unless it is newer
+    than every source. Returns its path."""
+    out = OUT_DEBUG if debug else OUT
+    if not force and up_to_date(out):
+        return out
+    tmp = out + ".tmp"
+    cmd = [nvcc(), *NVCC_FLAGS, *(["-DGQA_DEBUG_CHECKS"] if debug else []), "-I", INCLUDE, "-o", tmp,
+           os.path.join(CSRC, "gqa_sm100.cu")]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)
-    os.replace(tmp, OUT)
-    return OUT
+    os.replace(tmp, out)
+    return out
 
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--force", action="store_true")
     ap.add_argument("-v", "--verbose", action="store_true")
+    ap.add_argument("--debug", action="store_true", help="build libgqa_sm100_debug.so (in-kernel checks)")
     a = ap.parse_args()
-    print(build(force=a.force, verbose=a.verbose))
+    print(build(force=a.force, verbose=a.verbose, debug=a.debug))
     sys.exit(0)

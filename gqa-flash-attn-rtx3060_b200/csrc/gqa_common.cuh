@@ -38,6 +38,17 @@ __device__ __forceinline__ void report_device_error(int code, int site) {
   if (atomicCAS(&g_device_error, 0, code) == 0) g_device_error_site = site;
 }
 
+// Debug builds (-DGQA_DEBUG_CHECKS, `build.py --debug`): the TMA, UMMA and TMEM
+// helpers below check their addresses and coordinates first. A failed check records
+// GQA_ERR_DEBUG_CHECK and a site id in the device error word and skips the access;
+// the wait that depended on it then expires (bounded), so a bad index becomes an
+// error status instead of a fault. Release builds compile the checks away.
+#ifdef GQA_DEBUG_CHECKS
+#define GQA_CHECK(cond, site) ((cond) ? true : (report_device_error(GQA_ERR_DEBUG_CHECK, (site)), false))
+#else
+#define GQA_CHECK(cond, site) true
+#endif
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -129,6 +140,8 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
 }
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0,
                                             int c1, int c2, int c3) {
+  // 128-byte swizzled tiles start on 128 bytes; x * 2 bytes is a multiple of 16.
+  if (!GQA_CHECK((dst & 127u) == 0 && (c0 & 7) == 0 && (bar & 7u) == 0, 900)) return;
   asm volatile(
       "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
@@ -137,6 +150,7 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
 }
 __device__ __forceinline__ void tma_load_4d_hint(uint32_t dst, const CUtensorMap* map, uint32_t bar,
                                                  int c0, int c1, int c2, int c3, uint64_t policy) {
+  if (!GQA_CHECK((dst & 127u) == 0 && (c0 & 7) == 0 && (bar & 7u) == 0, 900)) return;
   asm volatile(
       "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
       " [%0], [%1, {%3, %4, %5, %6}], [%2], %7;" ::"r"(dst),
@@ -155,6 +169,8 @@ __device__ __forceinline__ uint64_t l2_policy_evict_first() {
 }
 __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, uint32_t src, int c0, int c1, int c2,
                                              int c3) {
+  // Stores never start at a negative coordinate.
+  if (!GQA_CHECK((src & 127u) == 0 && (c0 & 7) == 0 && c0 >= 0 && c1 >= 0 && c2 >= 0 && c3 >= 0, 901)) return;
   asm volatile(
       "cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
           reinterpret_cast<uint64_t>(map)),
@@ -185,6 +201,7 @@ __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.
 // D[tmem] (+)= A[smem] * B[smem]   (kind::f16: f16/bf16 inputs, f32 accumulate)
 __device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                         uint32_t accumulate) {
+  if (!GQA_CHECK((d_tmem & 0xFFFFu) < 512u, 903)) return;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
@@ -195,6 +212,7 @@ __device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a_desc, uint64
 // D[tmem] (+)= A[tmem] * B[smem]
 __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
                                         uint32_t accumulate) {
+  if (!GQA_CHECK((d_tmem & 0xFFFFu) < 512u && (a_tmem & 0xFFFFu) < 512u, 903)) return;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
@@ -221,12 +239,14 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N, bool bf16, b
 //   [46,48) version = 1; [49,52) base offset = 0 (tiles are 1024-byte aligned); [61,64) layout = 2 (SW128).
 // K-major operand: rows of 128 bytes, 8-row groups 1024 bytes apart (SBO); LBO unused.
 __device__ __forceinline__ uint64_t desc_sw128_kmajor(uint32_t saddr) {
+  (void)GQA_CHECK((saddr & 15u) == 0, 902);
   return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 // MN-major operand: each 128-byte row holds 64 MN-contiguous elements of one K index;
 // consecutive 64-element MN blocks are `lbo_bytes` apart, 8-row K groups 1024 bytes apart.
 __device__ __forceinline__ uint64_t desc_sw128_mnmajor(uint32_t saddr, uint32_t lbo_bytes) {
+  (void)GQA_CHECK((saddr & 15u) == 0 && (lbo_bytes & 15u) == 0, 902);
   return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16) |
          ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
@@ -239,6 +259,7 @@ __device__ __forceinline__ uint64_t desc_sw128_mnmajor(uint32_t saddr, uint32_t 
                      "r"(p[o + 5]), "r"(p[o + 6]), "r"(p[o + 7])
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+  if (!GQA_CHECK((taddr & 0xFFFFu) + 32u <= 512u, 904)) return;  // warp-uniform address
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
       "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -247,6 +268,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+  if (!GQA_CHECK((taddr & 0xFFFFu) + 16u <= 512u, 904)) return;  // warp-uniform address
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
       "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
@@ -254,6 +276,7 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
+  if (!GQA_CHECK((taddr & 0xFFFFu) + 32u <= 512u, 904)) return;
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
       "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
@@ -262,6 +285,7 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
       : "memory");
 }
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+  if (!GQA_CHECK((taddr & 0xFFFFu) + 16u <= 512u, 904)) return;
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
       "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),

@@ -445,7 +445,7 @@ __global__ void __launch_bounds__(384, 1)
       split = wk2.split;
       n_valid = wk2.n_valid;
     }
-    float w_own = 1.0f, inv = 1.0f / l_run;  // l == 0 -> inf -> NaN rows, the reference's 0/0
+    float inv = 1.0f / l_run;  // l == 0 -> inf -> NaN rows, the reference's 0/0
     float m_ref = 0.f;                       // reference max of the combined splits
     bool store = true;
     int n_other = 0;
@@ -499,8 +499,10 @@ __global__ void __launch_bounds__(384, 1)
             if (s0 + i < n_valid && s0 + i != split) M = fmaxf(M, mv[i]);
         }
         const float Mu = (M == -INFINITY) ? 0.f : M;
-        w_own = fast_exp2(m_run - Mu);
-        float L = w_own * l_run;
+        // L = sum over splits in split order (this CTA's own terms from registers, the
+        // same values it published), so the result does not depend on which CTA of the
+        // unit arrives last.
+        float L = 0.f;
         for (int s0 = 0; s0 < n_valid; s0 += 4) {
           float mv[4], lv[4];
 #pragma unroll
@@ -510,8 +512,11 @@ __global__ void __launch_bounds__(384, 1)
             lv[i] = __ldcg(p.ws_l + o2);
           }
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            if (s0 + i < n_valid && s0 + i != split) L += fast_exp2(mv[i] - Mu) * lv[i];
+          for (int i = 0; i < 4; ++i) {
+            if (s0 + i >= n_valid) continue;
+            const bool own = s0 + i == split;
+            L += fast_exp2((own ? m_run : mv[i]) - Mu) * (own ? l_run : lv[i]);
+          }
         }
         inv = 1.0f / L;
         n_other = n_valid - 1;
@@ -531,22 +536,28 @@ __global__ void __launch_bounds__(384, 1)
         for (int e = 0; e < 32; ++e) orr[e] = __float_as_uint(__int_as_float(0x7fc00000));
       }
       if (n_other > 0) {
+        // Fold the splits in split order, two per pass (64 independent loads in flight
+        // per thread); this CTA's own split comes from its TMEM values. An index past
+        // the last split reads a valid partial at weight 0.
+        uint32_t own[32];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) orr[e] = __float_as_uint(w_own * __uint_as_float(orr[e]));
-        // Two other splits per pass: 64 independent loads in flight per thread. An index
-        // past the last split or equal to this CTA's own reads a valid partial at weight 0.
+        for (int e = 0; e < 32; ++e) {
+          own[e] = orr[e];
+          orr[e] = 0u;
+        }
         for (int s0 = 0; s0 < n_valid; s0 += 2) {
           const int sa = s0, sb = min(s0 + 1, n_valid - 1);
-          const float wa = (sa == split) ? 0.f : fast_exp2(__ldcg(p.ws_m + pbase + (int64_t)sa * 256) - m_ref);
-          const float wb = (s0 + 1 >= n_valid || sb == split)
-                               ? 0.f : fast_exp2(__ldcg(p.ws_m + pbase + (int64_t)sb * 256) - m_ref);
+          const float ma = (sa == split) ? m_run : __ldcg(p.ws_m + pbase + (int64_t)sa * 256);
+          const float mb = (sb == split) ? m_run : __ldcg(p.ws_m + pbase + (int64_t)sb * 256);
+          const float wa = fast_exp2(ma - m_ref);
+          const float wb = (s0 + 1 >= n_valid) ? 0.f : fast_exp2(mb - m_ref);
           const float* xa = p.ws_acc + ((int64_t)unit * p.nsplit + sa) * HD * 256 + prow + c * 32 * 256;
           const float* xb = p.ws_acc + ((int64_t)unit * p.nsplit + sb) * HD * 256 + prow + c * 32 * 256;
           float va[32], vb[32];
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
-            va[e] = __ldcg(xa + e * 256);
-            vb[e] = __ldcg(xb + e * 256);
+            va[e] = (sa == split) ? __uint_as_float(own[e]) : __ldcg(xa + e * 256);
+            vb[e] = (sb == split) ? __uint_as_float(own[e]) : __ldcg(xb + e * 256);
           }
 #pragma unroll
           for (int e = 0; e < 32; ++e)

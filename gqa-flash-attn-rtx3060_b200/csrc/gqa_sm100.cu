@@ -380,6 +380,7 @@ const char* gqa_strerror(int code) {
     case GQA_ERR_NO_DEVICE: return "no sm_100 (B200) device is current";
     case GQA_ERR_SCRATCH_LIMIT: return "problem needs more scratch than the static no-allocation buffer "
                                        "(GQA_NOALLOC_SCRATCH_BYTES) holds";
+    case GQA_ERR_DEBUG_CHECK: return "a debug build's in-kernel address or coordinate check failed (access skipped)";
     default: return "unknown gqa status code";
   }
 }

@@ -11,7 +11,12 @@ import threading
 import torch
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libgqa_sm100.so")
+# GQA_KERNELS_LIB=debug selects the checked build (build.py --debug), whose kernels
+# report a bad address or coordinate as GQA_ERR_DEBUG_CHECK instead of faulting;
+# any other value is taken as a path.
+_SEL = os.environ.get("GQA_KERNELS_LIB", "")
+LIB_PATH = (os.path.join(_HERE, "libgqa_sm100_debug.so") if _SEL == "debug"
+            else _SEL if _SEL else os.path.join(_HERE, "libgqa_sm100.so"))
 
 GQA_DTYPE_F16 = 0
 GQA_DTYPE_BF16 = 1

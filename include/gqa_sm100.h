@@ -40,6 +40,7 @@ extern "C" {
 #define GQA_ERR_WORKSPACE 6     /* workspace missing or too small              */
 #define GQA_ERR_NO_DEVICE 7     /* no sm_100 device current                    */
 #define GQA_ERR_SCRATCH_LIMIT 8 /* problem needs more than the static scratch  */
+#define GQA_ERR_DEBUG_CHECK 9   /* a debug build's address/coordinate check failed (device error word) */
 
 #define GQA_DTYPE_F16 0
 #define GQA_DTYPE_BF16 1

@@ -29,6 +29,16 @@ def test_library_exports_every_declared_symbol(lib_path):
     assert not missing, missing
 
 
+def test_debug_library_exports_every_declared_symbol(lib_path):
+    """The checked variant (build.py --debug) has the same C ABI."""
+    path = os.path.join(os.path.dirname(lib_path), "libgqa_sm100_debug.so")
+    if not os.path.exists(path):
+        pytest.skip("debug variant not built")
+    lib = ctypes.CDLL(path)
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
 def test_binding_covers_the_header(lib_path):
     from gqa_kernels import _lib
     assert sorted(_lib.SIGNATURES) == declared_functions()

@@ -210,3 +210,13 @@ def test_unsupported_inputs_raise():
 def test_no_device_error_recorded():
     torch.cuda.synchronize()
     assert check_device_error() == (0, 0)
+
+
+@pytest.mark.parametrize("shape", [(4, 4, 1, 512, 16384, 128),   # prefill key split (last-CTA combine)
+                                   (1, 32, 8, 1, 16384, 128)])   # split-KV decode (last-CTA combine)
+def test_split_paths_are_deterministic(shape):
+    """Which CTA of a unit arrives last varies from run to run; the combine must not."""
+    q, k, v = (t.to(DEVICE) for t in make_inputs(*shape, seed=31))
+    first = gqa_flash_attn(q, k, v, causal=True)
+    for _ in range(4):
+        assert torch.equal(gqa_flash_attn(q, k, v, causal=True).view(torch.int16), first.view(torch.int16))
