@@ -11,10 +11,18 @@ from . import _lib
 from .gqa_fwd import gqa_fwd_kernel
 from .gqa_split import split_kv_forward
 
-__all__ = ["gqa_flash_attn"]
+__all__ = ["gqa_flash_attn", "set_nvtx_ranges"]
 
 SM_COUNT = 28  # routing constant of the reference (dispatch.py:10); launches use the real SM count
 LOG2E = 1.4426950408889634
+_NVTX = False
+
+
+def set_nvtx_ranges(enabled=True):
+    """Wrap every gqa_flash_attn call in an NVTX range named after its path and shape
+    (visible in Nsight timelines); off by default, when a call pays one flag test."""
+    global _NVTX
+    _NVTX = bool(enabled)
 
 
 def _cdiv(a, b):
@@ -39,6 +47,18 @@ def gqa_flash_attn(q, k, v, causal=True):
     Returns:
         (batch, num_heads, seq_q, head_dim), same dtype as q.
     """
+    if not _NVTX:
+        return _gqa_flash_attn(q, k, v, causal)
+    b, hq, sq, d = q.shape
+    torch.cuda.nvtx.range_push(f"gqa_flash_attn b{b} hq{hq} hkv{k.shape[1]} sq{sq} skv{k.shape[2]} d{d}")
+    try:
+        return _gqa_flash_attn(q, k, v, causal)
+    finally:
+        torch.cuda.nvtx.range_pop()
+
+
+def _gqa_flash_attn(q, k, v, causal=True):
+    """The call itself (routing and launch); see gqa_flash_attn."""
     batch, num_heads, seq_q, head_dim = q.shape
     _, num_kv_heads, seq_kv, _ = k.shape
     assert num_heads % num_kv_heads == 0, "num_heads must be divisible by num_kv_heads"

@@ -220,3 +220,15 @@ def test_split_paths_are_deterministic(shape):
     first = gqa_flash_attn(q, k, v, causal=True)
     for _ in range(4):
         assert torch.equal(gqa_flash_attn(q, k, v, causal=True).view(torch.int16), first.view(torch.int16))
+
+
+def test_nvtx_ranges_do_not_change_results():
+    import gqa_kernels
+    q, k, v = (t.to(DEVICE) for t in make_inputs(1, 32, 8, 300, 300, 128, seed=32))
+    plain = gqa_flash_attn(q, k, v, causal=True)
+    gqa_kernels.set_nvtx_ranges(True)
+    try:
+        ranged = gqa_flash_attn(q, k, v, causal=True)
+    finally:
+        gqa_kernels.set_nvtx_ranges(False)
+    assert torch.equal(plain.view(torch.int16), ranged.view(torch.int16))
