@@ -20,6 +20,13 @@
 // CTA ends at the last key any of its rows can see; row r masks keys beyond
 // its own position + (seq_kv - seq_q). Only the last one or two key tiles of a
 // CTA need the mask.
+//
+// Paged K/V (PAGED): K and V come from vLLM-layout block caches. The producer
+// loads each 128-key tile as two 64-key boxes, each from the physical block the
+// sequence's block table names; a box past the sequence's end gets an
+// out-of-range block coordinate, so TMA fills it with zeros. Each sequence has
+// its own length (read after the grid dependency wait) and so its own causal
+// offset; the tile plan is made for the host's bound of the lengths.
 #pragma once
 
 #include "gqa_common.cuh"
@@ -30,6 +37,13 @@ struct PrefillParams {
   int batch, hq, hkv, group, seq_q, seq_kv;
   int bm;       // positions per tile = 128 / group
   int n_pairs;  // ceil(ceil(seq_q / bm) / 2)
+  // Unit order. Pair-major (unit_inner = batch * hkv): the longest query pairs of all
+  // (batch, kv head) first, which balances causal work. Head-major (unit_inner =
+  // n_pairs): the pairs of one (batch, kv head) side by side, so the CTAs reading the
+  // same keys and values run together and share them in L2; the host picks it when
+  // the pairs' key counts are within a factor of two.
+  int head_major;
+  int unit_inner;
   int causal;
   float scale_log2;
   // Key-axis split of each unit (query pair of one (batch, kv head)) across
@@ -43,10 +57,20 @@ struct PrefillParams {
   float* ws_l;
   float* ws_acc;
   unsigned* ws_cnt;
+  // Paged K/V (the PAGED instantiation): the caches are [num_blocks][block_size][hkv][HD];
+  // key k of sequence b sits in physical block block_table[b * bt_stride + (k >> block_shift)]
+  // at position k & (block_size - 1), and the sequence holds min(seq_lens[b], seq_kv) keys
+  // (seq_kv is then the host's bound of the lengths). Query position i of sequence b is
+  // key position len_b - seq_q + i (bottom-right alignment per sequence).
+  const int* block_table;
+  const int* seq_lens;
+  int bt_stride;
+  int block_shift;
+  int num_blocks;
 };
 
-// Work item of CTA `cta`: unit = (query pair, batch, kv head), longest pair first;
-// split = which chunk of the unit's key tiles. A unit with fewer key tiles than
+// Work item of CTA `cta`: unit = (query pair, batch, kv head) in the order above,
+// longest pair of a head first; split = which chunk of the unit's key tiles. A unit with fewer key tiles than
 // the splits cover uses fewer splits (n_valid); the others return at once.
 struct PrefillWork {
   int unit, split, n_valid, b, kvh, p0, j0, nk;
@@ -61,9 +85,10 @@ __device__ __forceinline__ PrefillWork prefill_work(const PrefillParams& p, unsi
   const unsigned unit = SPLIT ? cta / (unsigned)p.nsplit : cta;
   w.split = SPLIT ? (int)(cta % (unsigned)p.nsplit) : 0;
   w.unit = (int)unit;
-  const int bh_count = p.batch * p.hkv;
-  const int bh = unit % bh_count;
-  const int pair = p.n_pairs - 1 - unit / bh_count;
+  const int inner = unit % p.unit_inner;
+  const int outer = unit / p.unit_inner;
+  const int bh = p.head_major ? outer : inner;
+  const int pair = p.n_pairs - 1 - (p.head_major ? inner : outer);
   w.b = bh / p.hkv;
   w.kvh = bh % p.hkv;
   w.p0 = pair * 2 * p.bm;  // first position of tile 0
@@ -75,6 +100,18 @@ __device__ __forceinline__ PrefillWork prefill_work(const PrefillParams& p, unsi
   w.j0 = (SPLIT && w.n_valid > 1) ? w.split * p.chunk_tiles : 0;  // key tiles [j0, j0 + nk)
   w.nk = (SPLIT && w.n_valid > 1) ? min(nk_unit, w.j0 + p.chunk_tiles) - w.j0 : nk_unit;
   return w;
+}
+
+// Key tiles of a paged work item once its sequence's length kv_len is known. The
+// plan (n_valid, j0) was made for the host's bound seq_kv; a split past a shorter
+// sequence's last tile gets none and publishes an empty partial.
+template <int BN>
+__device__ __forceinline__ int paged_work_tiles(const PrefillParams& p, const PrefillWork& w, int kv_len) {
+  int kv_end = kv_len;
+  if (p.causal) kv_end = min(kv_end, min(w.p0 + 2 * p.bm, p.seq_q) + kv_len - p.seq_q);
+  const int nk_unit = (kv_end > 0) ? (kv_end + BN - 1) / BN : 0;
+  if (w.n_valid > 1) return max(0, min(nk_unit, w.j0 + p.chunk_tiles) - w.j0);
+  return nk_unit;
 }
 
 template <int HD>
@@ -90,8 +127,9 @@ struct PrefillCfg {
   static constexpr int kBarOff = kKVOff + kSlots * kTileBytes;
   // barriers: q_full[2] kv_full[S] kv_empty[S] s_full[2] p_full[2 tiles][2 halves] o_final[2] mma_done
   static constexpr int kNumBars = 2 + 2 * kSlots + 2 + 4 + 2 + 1;
-  static constexpr int kMiscOff = kBarOff + kNumBars * 8;  // tmem base, abort flag
-  static constexpr int kSmemBytes = kMiscOff + 16 + 1024;  // + alignment slack
+  // tmem base, abort flag, last-CTA flag, paged key tiles, paged sequence length
+  static constexpr int kMiscOff = kBarOff + kNumBars * 8;
+  static constexpr int kSmemBytes = kMiscOff + 32 + 1024;  // + alignment slack
   // warps 0-3 softmax tile 0, 4-7 softmax tile 1, 8 MMA issuer, 9 TMA producer, 10-11 idle
   static constexpr int kThreads = 384;
   static constexpr int kTmemCols = 512;
@@ -108,7 +146,7 @@ struct PrefillCfg {
   static constexpr int kMufuPairsPer8 = 7;
 };
 
-template <int HD, bool BF16, bool SPLIT>
+template <int HD, bool BF16, bool SPLIT, bool PAGED = false>
 __global__ void __launch_bounds__(384, 1)
     gqa_prefill_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap qmap,
                        const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
@@ -142,8 +180,19 @@ __global__ void __launch_bounds__(384, 1)
   // ---- work item: longest (highest) query pair first, across all (b, kv) ----
   const PrefillWork wk = prefill_work<Cfg::kBN, SPLIT>(p, blockIdx.x);
   if (wk.split >= wk.n_valid) return;  // whole CTA, before any barrier or TMEM use
-  const int b = wk.b, kvh = wk.kvh, p0 = wk.p0, j0 = wk.j0, nk = wk.nk;
-  const int off = p.seq_kv - p.seq_q;
+  const int b = wk.b, kvh = wk.kvh, p0 = wk.p0, j0 = wk.j0;
+  // A paged CTA's key tiles and sequence length depend on a value read from global
+  // memory; they are kept in shared memory (written by thread 0 before the CTA
+  // barrier below) and read where used, rather than held in registers across the
+  // loops: the softmax warps have none to spare, and the dense values are
+  // recomputed from parameters instead.
+  volatile int* const paged_info = reinterpret_cast<volatile int*>(smem + Cfg::kMiscOff + 12);
+  auto work_tiles = [&]() -> int {
+    if constexpr (PAGED) return paged_info[0]; else return wk.nk;
+  };
+  auto seq_len = [&]() -> int {
+    if constexpr (PAGED) return paged_info[1]; else return p.seq_kv;
+  };
 
   if (tid == 0) {
     mbar_init(bar_q_full, 1);
@@ -167,6 +216,13 @@ __global__ void __launch_bounds__(384, 1)
   // the stream has finished (programmatic dependent launch).
   pdl_wait();
   pdl_trigger();
+  if constexpr (PAGED) {
+    if (tid == 0) {
+      const int len = max(0, min(p.seq_lens[b], p.seq_kv));
+      paged_info[1] = len;
+      paged_info[0] = paged_work_tiles<Cfg::kBN>(p, wk, len);
+    }
+  }
   if (warp == 8) {
     tmem_alloc(smem_u32(tmem_base_ptr), Cfg::kTmemCols);
     tmem_relinquish();
@@ -183,6 +239,8 @@ __global__ void __launch_bounds__(384, 1)
     asm volatile("setmaxnreg.dec.sync.aligned.u32 88;" ::: "memory");
   if (warp == 9) {
     // ================================================================ producer
+    const int nk = work_tiles();
+    const int kv_len = seq_len();
     if (lane == 0 && nk > 0) {
       tma_prefetch_desc(&qmap);
       tma_prefetch_desc(&kmap);
@@ -198,17 +256,40 @@ __global__ void __launch_bounds__(384, 1)
       }
       int t = 0;
       const int n_loads = 2 * nk;
+      int pb0 = 0, pb1 = 0;  // paged: physical blocks of the tile's two 64-key boxes
       for (; t < n_loads; ++t) {
         const int slot = t % SLOTS;
         const int use = t / SLOTS;
+        const int key0 = (j0 + (t >> 1)) * Cfg::kBN;
+        if constexpr (PAGED) {
+          // Looked up once per tile (K loads; V reuses them) and before the slot
+          // wait, so the table read overlaps it.
+          if ((t & 1) == 0) {
+            const int* row_bt = p.block_table + (int64_t)b * p.bt_stride;
+            pb0 = (key0 < kv_len) ? row_bt[key0 >> p.block_shift] : p.num_blocks;
+            pb1 = (key0 + 64 < kv_len) ? row_bt[(key0 + 64) >> p.block_shift] : p.num_blocks;
+          }
+        }
         if (use > 0 && !mbar_wait(bar_kv_empty + 8 * slot, (use - 1) & 1, abort_flag, 1)) break;
         const uint32_t full = bar_kv_full + 8 * slot;
         mbar_arrive_expect_tx(full, Cfg::kTileBytes);
         const CUtensorMap* map = (t & 1) ? &vmap : &kmap;
-        const int key0 = (j0 + (t >> 1)) * Cfg::kBN;
+        if constexpr (PAGED) {
+          // Map (d, kv head, position in block, block), box {64, 1, 64, 1}: 64 rows of
+          // 128 bytes, so the two boxes of a sub-tile form its 128 swizzled rows.
+          const int pos0 = key0 & ((1 << p.block_shift) - 1);
 #pragma unroll
-        for (int s = 0; s < NSUB; ++s)
-          tma_load_4d(kv_smem0 + slot * Cfg::kTileBytes + s * Cfg::kSubBytes, map, full, s * 64, key0, kvh, b);
+          for (int s = 0; s < NSUB; ++s) {
+            const uint32_t dst = kv_smem0 + slot * Cfg::kTileBytes + s * Cfg::kSubBytes;
+            tma_load_4d(dst, map, full, s * 64, kvh, pos0, pb0);
+            tma_load_4d(dst + Cfg::kSubBytes / 2, map, full, s * 64, kvh,
+                        (key0 + 64) & ((1 << p.block_shift) - 1), pb1);
+          }
+        } else {
+#pragma unroll
+          for (int s = 0; s < NSUB; ++s)
+            tma_load_4d(kv_smem0 + slot * Cfg::kTileBytes + s * Cfg::kSubBytes, map, full, s * 64, key0, kvh, b);
+        }
       }
       if (t < n_loads) {  // aborted: let in-flight loads land before teardown
         volatile int dummy = 0;
@@ -218,6 +299,7 @@ __global__ void __launch_bounds__(384, 1)
     }
   } else if (warp == 8) {
     // ================================================================ MMA issuer
+    const int nk = work_tiles();
     if (lane == 0 && nk > 0) {
       constexpr uint32_t idesc_qk = make_idesc_f16(128, Cfg::kBN, BF16, false);
       constexpr uint32_t idesc_pv = make_idesc_f16(128, HD, BF16, true);
@@ -309,21 +391,25 @@ __global__ void __launch_bounds__(384, 1)
 
     const int g = row / p.bm;
     const int pos = p0 + wg * p.bm + (row - g * p.bm);
-    int lim = p.seq_kv;  // number of keys this row may see
-    if (p.causal) lim = min(lim, pos + off + 1);
-    lim -= j0 * Cfg::kBN;  // counted from this CTA's first key tile
+    // Number of keys this row may see, counted from this CTA's first key tile.
+    auto row_lim = [&]() -> int {
+      const int len = seq_len();
+      const int lim = p.causal ? min(len, pos + len - p.seq_q + 1) : len;
+      return lim - j0 * Cfg::kBN;
+    };
     const float scale = p.scale_log2;
 
     // A row that sees no key at all keeps m = -inf, and its NaN (exp2(-inf + inf))
     // reaches the output, as in the reference. Such rows only occur in units of at
-    // most two key tiles, which are never split. In a split unit a row may see no
+    // most two key tiles, which are never split (paged sequences shorter than the
+    // plan's bound excepted: the combine marks them). In a split unit a row may see no
     // key of this CTA's chunk while it sees keys of others: a finite start value
     // keeps its P finite (exp2(-inf + 3e38) = 0), and the combine gives the chunk
     // the weight exp2(-3e38 - M) = 0.
     float m_run = (wk.n_valid > 1) ? -3.0e38f : -INFINITY;
     float l_run = 0.f;
     bool ok = true;
-    for (int j = 0; j < nk; ++j) {
+    for (int j = 0; j < work_tiles(); ++j) {
       ok = mbar_wait(s_full, j & 1, abort_flag, 20 + wg);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
@@ -337,7 +423,7 @@ __global__ void __launch_bounds__(384, 1)
       reg_fence_n<64>(sr);
       tmem_ld32(tS + 64, sr + 64);
       tmem_ld32(tS + 96, sr + 96);
-      const int rem = lim - j * Cfg::kBN;  // visible columns in this tile
+      const int rem = row_lim() - j * Cfg::kBN;  // visible columns in this tile
       const bool masked = rem < Cfg::kBN;
       if (masked) {
 #pragma unroll
@@ -425,7 +511,7 @@ __global__ void __launch_bounds__(384, 1)
     }
 
     // ---- epilogue: O / l -> 16-bit -> swizzled staging (this tile's Q buffer) -> TMA store
-    bool have_o = ok && nk > 0;
+    bool have_o = ok && work_tiles() > 0;
     if (have_o) {
       have_o = mbar_wait(bar_o_final + 8 * wg, 0, abort_flag, 22 + wg);
       have_o = __all_sync(0xffffffffu, have_o);
@@ -466,7 +552,7 @@ __global__ void __launch_bounds__(384, 1)
           reg_fence(orr);
         } else {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) orr[e] = __float_as_uint(__int_as_float(0x7fc00000));
+          for (int e = 0; e < 32; ++e) orr[e] = (PAGED && work_tiles() == 0) ? 0u : 0x7fc00000u;  // empty split: 0
         }
 #pragma unroll
         for (int e = 0; e < 32; ++e) __stcg(acc_own + (c * 32 + e) * 256, __uint_as_float(orr[e]));
@@ -519,6 +605,11 @@ __global__ void __launch_bounds__(384, 1)
           }
         }
         inv = 1.0f / L;
+        if constexpr (PAGED) {
+          // A paged sequence shorter than the chunk has rows that see no key in any
+          // split (every m still at its start value): NaN, as in the reference.
+          if (M == -3.0e38f) inv = __int_as_float(0x7fc00000);
+        }
         n_other = n_valid - 1;
         m_ref = Mu;
       }
@@ -533,7 +624,7 @@ __global__ void __launch_bounds__(384, 1)
         reg_fence(orr);
       } else {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) orr[e] = __float_as_uint(__int_as_float(0x7fc00000));
+        for (int e = 0; e < 32; ++e) orr[e] = (PAGED && work_tiles() == 0) ? 0u : 0x7fc00000u;  // empty split: 0
       }
       if (n_other > 0) {
         // Fold the splits in split order, two per pass (64 independent loads in flight

@@ -60,7 +60,8 @@ struct StreamParams {
   // (the K/V tensor maps are (HD, hkv, block_size, num_blocks)); sequence b's key k lives
   // in physical block block_table[b * bt_stride + (k >> block_shift)] at position
   // k & (block_size - 1), and the sequence holds seq_lens[b] keys. block_size is a power
-  // of two >= 64, so a 64-key box never crosses a block.
+  // of two >= 64, so a 64-key box never crosses a block. The sequence's seq_q queries
+  // are its last seq_q positions (causal offset seq_lens[b] - seq_q).
   const int* block_table;
   const int* seq_lens;
   int bt_stride;
@@ -121,7 +122,7 @@ __global__ void __launch_bounds__(288, 1)
   const int mt = unit % p.n_mtiles;
   const int kvh = (unit / p.n_mtiles) % p.hkv;
   const int b = unit / (p.n_mtiles * p.hkv);
-  const int off = p.seq_kv_total - p.seq_q;  // bottom-right causal offset (global)
+  int off = p.seq_kv_total - p.seq_q;  // bottom-right causal offset (global; paged: per sequence)
   const bool paged = p.block_table != nullptr;
 
   // The producer thread initialises the barriers; every thread then waits for the
@@ -144,7 +145,10 @@ __global__ void __launch_bounds__(288, 1)
 
   // Highest key (local, exclusive) any valid row of this unit may see.
   int kv_end = p.seq_kv;
-  if (paged) kv_end = min(kv_end, p.seq_lens[b]);
+  if (paged) {
+    kv_end = max(0, min(kv_end, p.seq_lens[b]));
+    off = kv_end - p.seq_q;  // the sequence's queries are its last seq_q positions
+  }
   if (p.causal) {
     const int last_pos = min((mt + 1) * p.block_m, p.seq_q) - 1;
     kv_end = min(kv_end, last_pos + off - p.kv_offset + 1);

@@ -186,6 +186,32 @@ int gqa_paged_decode(const void* q, const void* k_cache, const void* v_cache, vo
                      void* stream);
 
 /*
+ * Paged forward (chunked prefill over a paged cache): each sequence's seq_q new
+ * query tokens attend to its cached keys, read from the same vLLM-layout caches
+ * as gqa_paged_decode. q/o are (num_seqs, num_heads, seq_q, head_dim) with
+ * element strides q_strides / o_strides (the gqa_fwd convention). The queries
+ * of sequence b are its last seq_q positions: with `causal`, query i sees keys
+ * [0, seq_lens[b] - seq_q + i] (bottom-right alignment per sequence, the dense
+ * path's rule); without, all seq_lens[b] keys. Rows that see no key give NaN.
+ * Short chunks (group * seq_q <= 64) run the streaming kernel, longer ones the
+ * tcgen05 prefill kernel, whose producer reads K/V tiles through the block
+ * table. Cache slots past seq_lens[b] in a sequence's last block are read and
+ * weighted 0, so they must hold finite values (a zero-initialised cache does).
+ * The key split is sized by max_seq_len; its workspace (zeroed before first
+ * use; every call leaves it zero) is gqa_paged_fwd_workspace_bytes(). Called
+ * with seq_q = 1 and causal = 0 this is gqa_paged_decode.
+ * No reference counterpart: the roadmap's vLLM-shaped interface (README.md:144)
+ * over the attention of gqa_kernels/gqa_fwd.py.
+ */
+size_t gqa_paged_fwd_workspace_bytes(int num_seqs, int num_heads, int num_kv_heads, int seq_q, int max_seq_len,
+                                     int head_dim);
+int gqa_paged_fwd(const void* q, const void* k_cache, const void* v_cache, void* o, const int64_t* q_strides,
+                  const int64_t* o_strides, const int* block_table, int bt_stride, const int* seq_lens,
+                  int num_seqs, int num_heads, int num_kv_heads, int seq_q, int head_dim, int block_size,
+                  int num_blocks, int max_seq_len, float scale_log2, int causal, int dtype, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
+/*
  * Reads (and clears, if `clear` is nonzero) the device error word of the
  * current device: 0, or GQA_ERR_TIMEOUT when a bounded in-kernel wait expired.
  * `site` (optional) receives the wait site id. Synchronises the current device.
