@@ -14,8 +14,8 @@ gather copy: their TMA producers map every 64-key box through the block table.
   the tcgen05 prefill kernel for long chunks, the streaming kernel for short
   ones (the reference's gqa_kernels/gqa_fwd.py attention).
 
-Cache slots past a sequence's length in its last block are read and weighted 0,
-so they must hold finite values (vLLM zero-initialises its caches).
+Cache slots past a sequence's length in its last block are read and masked, so
+they must hold finite values (vLLM zero-initialises its caches).
 """
 import ctypes
 

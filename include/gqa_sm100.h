@@ -196,7 +196,7 @@ int gqa_paged_decode(const void* q, const void* k_cache, const void* v_cache, vo
  * Short chunks (group * seq_q <= 64) run the streaming kernel, longer ones the
  * tcgen05 prefill kernel, whose producer reads K/V tiles through the block
  * table. Cache slots past seq_lens[b] in a sequence's last block are read and
- * weighted 0, so they must hold finite values (a zero-initialised cache does).
+ * masked, so they must hold finite values (a zero-initialised cache does).
  * The key split is sized by max_seq_len; its workspace (zeroed before first
  * use; every call leaves it zero) is gqa_paged_fwd_workspace_bytes(). Called
  * with seq_q = 1 and causal = 0 this is gqa_paged_decode.
