@@ -1,7 +1,7 @@
 """Benchmark of the B200 GQA flash-attention forward (driver contract).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|sdpa|flash_attn]
-                    [--workload prefill|decode|chunked|long_decode]
+                    [--workload prefill|decode|chunked|long_decode|paged_decode|paged_decode_fp8]
 
 Default workload (BASELINE metric "prefill TFLOP/s @8K causal; decode HBM GB/s
 & us @16K KV"): Llama-3.1-8B-shape causal prefill B=1 per GPU, Hq=32, Hkv=8,
@@ -27,6 +27,10 @@ same workload; under torchrun only rank 0 runs it. --impl sdpa and --impl
 flash_attn time same-box library comparators (torch SDPA, flash_attn 2) on the
 same workloads and timing, the role the reference's benchmark/run.py gives
 SDPA and FA2; their lines carry "impl" and report no launches of this library.
+
+--workload paged_decode / paged_decode_fp8 time decode over a vLLM-layout paged
+cache (gqa_kernels.paged) with bf16 or e4m3 K/V, config 3's shape for 8
+sequences; `value` counts K/V at the cache's element size.
 """
 import argparse
 import datetime
@@ -78,7 +82,20 @@ WORKLOADS = {
                     name="chunked-prefill-b4-512x16k (config 4), batch x kv-head sharded"),
     "long_decode": dict(B=64, Hq=64, Hkv=8, Sq=1, Skv=131072, D=128, bound="hbm", scaling="strong",
                         name="long-decode-b64-131k (config 5), seq_kv sharded + NCCL LSE combine"),
+    # Paged-cache decode (gqa_kernels.paged): config 3's shape for 8 sequences, vLLM
+    # cache layout with 256-key blocks in shuffled order; bf16 or e4m3 K/V.
+    "paged_decode": dict(B=8, Hq=32, Hkv=8, Sq=1, Skv=16384, D=128, bound="hbm", scaling="weak", kv="bf16",
+                         name="paged-decode-8x16k (config 3 shape x 8 sequences, bf16 cache, block 256)"),
+    "paged_decode_fp8": dict(B=8, Hq=32, Hkv=8, Sq=1, Skv=16384, D=128, bound="hbm", scaling="weak", kv="fp8",
+                             name="paged-decode-fp8-8x16k (config 3 shape x 8 sequences, e4m3 cache, block 256)"),
 }
+
+
+def wl_bytes(wl):
+    """Compulsory HBM bytes of one workload instance (K/V at the cache's element size)."""
+    B, Hq, Hkv, Sq, Skv, D = wl["B"], wl["Hq"], wl["Hkv"], wl["Sq"], wl["Skv"], wl["D"]
+    kv_elem = 1 if wl.get("kv") == "fp8" else 2
+    return float(kv_elem * 2 * B * Hkv * Skv * D + 2 * 2 * B * Hq * Sq * D)
 
 
 def measured_peaks():
@@ -289,7 +306,7 @@ def run_attention_workload(wl, world, rank, device, steps, warmup, args):
     dt = torch.bfloat16
     gen = torch.Generator(device=device).manual_seed(rank)
     flops_total = attn_flops(B, Hq, Sq, Skv, D) * (world if wl["scaling"] == "weak" else 1)
-    bytes_total = attn_bytes(B, Hq, Hkv, Sq, Skv, D) * (world if wl["scaling"] == "weak" else 1)
+    bytes_total = wl_bytes(wl) * (world if wl["scaling"] == "weak" else 1)
 
     def rnd(*shape):
         return torch.randn(*shape, generator=gen, device=device, dtype=torch.float32).to(dt)
@@ -303,18 +320,39 @@ def run_attention_workload(wl, world, rank, device, steps, warmup, args):
             local["o"] = attn(local["q"], local["k"], local["v"])
         flush = make_flush(device)
         launches_per_step = 1
-    elif name == "decode":
-        # K+V (67 MB) fit in L2, so four input copies rotate (268 MB) instead of a flush.
-        # A serving loop replays its decode steps from CUDA graphs: here graphs of up to
-        # 16 consecutive steps (cycling the copies), so consecutive kernels overlap
-        # launch and prologue (programmatic dependent launch). Captured after a warm-up
-        # on the capture stream, so the split workspace is cached and none is allocated.
-        sets = [(rnd(B, Hq, Sq, D), rnd(B, Hkv, Skv, D), rnd(B, Hkv, Skv, D)) for _ in range(4)]
+    elif name in ("decode", "paged_decode", "paged_decode_fp8"):
+        # Dense decode: K+V (67 MB) fit in L2, so four input copies rotate (268 MB)
+        # instead of a flush. Paged decode: two cache copies of 268 MB (bf16) or 134 MB
+        # (e4m3) rotate. A serving loop replays its decode steps from CUDA graphs: here
+        # graphs of up to 16 consecutive steps (cycling the copies), so consecutive
+        # kernels overlap launch and prologue (programmatic dependent launch). Captured
+        # after a warm-up on the capture stream, so the split workspace is cached and
+        # none is allocated.
+        if name == "decode":
+            sets = [(rnd(B, Hq, Sq, D), rnd(B, Hkv, Skv, D), rnd(B, Hkv, Skv, D)) for _ in range(4)]
+
+            def call(i):
+                return attn(*sets[i % len(sets)])
+            local["q"], local["k"], local["v"] = sets[0]
+        else:
+            if args.impl != "ours":
+                raise SystemExit("the paged workloads run this library only")
+            from gqa_kernels.paged import paged_decode
+            bs, nb = 256, B * Skv // 256
+            kv_dt = torch.float8_e4m3fn if wl["kv"] == "fp8" else dt
+            sets = []
+            for _ in range(2):
+                bt = torch.randperm(nb, generator=gen, device=device).to(torch.int32).view(B, Skv // bs)
+                sets.append((rnd(B, Hq, D), rnd(nb, bs, Hkv, D).to(kv_dt), rnd(nb, bs, Hkv, D).to(kv_dt), bt,
+                             torch.full((B,), Skv, dtype=torch.int32, device=device)))
+
+            def call(i):
+                return paged_decode(*sets[i % len(sets)])
         gs = torch.cuda.Stream(device)
         gs.wait_stream(torch.cuda.current_stream(device))
         with torch.cuda.stream(gs):
-            for q, k, v in sets:
-                attn(q, k, v)
+            for i in range(len(sets)):
+                call(i)
         gs.synchronize()
         graphs = {}
 
@@ -323,11 +361,9 @@ def run_attention_workload(wl, world, rank, device, steps, warmup, args):
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.stream(gs), torch.cuda.graph(g, stream=gs):
                     for i in range(n):
-                        q, k, v = sets[i % len(sets)]
-                        local["o"] = attn(q, k, v)
+                        local["o"] = call(i)
                 graphs[n] = g
             return graphs[n]
-        local["q"], local["k"], local["v"] = sets[0]
 
         def step(n):  # runs n consecutive steps
             while n > 0:
@@ -372,7 +408,7 @@ def run_attention_workload(wl, world, rank, device, steps, warmup, args):
     clock = ClockSampler(device) if rank == 0 else None
     if clock:
         clock.start()
-    if name == "decode":
+    if name in ("decode", "paged_decode", "paged_decode_fp8"):
         graph_of(16), graph_of(steps % 16 or 16)  # capture outside the timed region
         times, wall = timed_loop(step, steps, warmup, world, device)
     else:
@@ -496,6 +532,7 @@ def cpu_sample(wl, budget_s, steps=None):
     n = 0
     per = []
     off = Skv - Sq
+    kv_elem = 1 if wl.get("kv") == "fp8" else 2  # bytes per cached K/V element of the workload
     while (steps is None and (elapsed < budget_s or n == 0)) or (steps is not None and n < steps):
         r0 = (n * rows * 37) % max(1, Sq - rows + 1) if Sq > rows else 0
         r1 = min(Sq, r0 + rows)
@@ -508,7 +545,7 @@ def cpu_sample(wl, budget_s, steps=None):
         elapsed += dt
         pairs = int(np.clip(np.arange(r0, r1) + off + 1, 0, Skv).sum())
         done_flops += 4.0 * G * D * pairs
-        done_bytes += 2.0 * (2 * kend * D + 2 * G * (r1 - r0) * D)
+        done_bytes += kv_elem * 2 * kend * D + 2.0 * 2 * G * (r1 - r0) * D
         n += 1
     if wl["bound"] == "tensor":
         val, unit = done_flops / elapsed / 1e12, "TFLOP/s"
@@ -536,7 +573,8 @@ def main():
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     wl = WORKLOADS[args.workload]
-    default_steps = {"prefill": 1000, "decode": 5000, "chunked": 500, "long_decode": 100}[args.workload]
+    default_steps = {"prefill": 1000, "decode": 5000, "chunked": 500, "long_decode": 100, "paged_decode": 2000,
+                     "paged_decode_fp8": 2000}[args.workload]
     steps = args.steps or default_steps
 
     if args.impl == "reference":
@@ -570,7 +608,7 @@ def main():
         "higher_is_better": True,
         "scaling": wl["scaling"],
         "vs_baseline": None,
-        "dtype": "bf16",
+        "dtype": "e4m3 K/V, f16 MMA, bf16 Q/O" if wl.get("kv") == "fp8" else "bf16",
         "data": "synthetic (N(0,1) bf16, CUDA generator seeded by rank)",
         "config": {"workload": wl["name"], "batch_per_gpu" if wl["scaling"] == "weak" else "batch": wl["B"],
                    "num_heads": wl["Hq"], "num_kv_heads": wl["Hkv"], "seq_q": wl["Sq"], "seq_kv": wl["Skv"],
@@ -578,6 +616,8 @@ def main():
                    "l2": "flushed between steps (256 MB write)" if args.workload in ("prefill", "chunked")
                    else "inputs larger than L2 (4 rotating copies, 268 MB); 16-step CUDA graphs back to back"
                    if args.workload == "decode"
+                   else "inputs larger than L2 (2 rotating caches); 16-step CUDA graphs back to back"
+                   if args.workload.startswith("paged")
                    else "inputs larger than L2 (32 GiB K/V)",
                    "parallelism": (f"batch-sharded x{world}" if wl["scaling"] == "weak" else
                                    f"kv-head/batch x{world}" if args.workload == "chunked" else
@@ -598,7 +638,7 @@ def main():
                             "peak_source": f"{peaks['source']} bf16 dense burst (MEASURED_PEAKS.json)",
                             "work_per_launch": work, "traffic": profile_traffic(args.workload)}
     else:
-        work = attn_bytes(wl["B"], wl["Hq"], wl["Hkv"], wl["Sq"], wl["Skv"], wl["D"]) * share
+        work = wl_bytes(wl) * share
         achieved = work / (launch_ms * 1e-3) / 1e9
         line["roofline"] = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm"], "unit": "GB/s",
                             "frac": round(achieved / peaks["hbm"], 4),

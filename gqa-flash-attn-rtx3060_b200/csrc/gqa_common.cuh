@@ -336,6 +336,34 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t&
                : "r"(addr));
 }
 
+// Two e4m3 values (low byte -> low half) to two f16, exactly (every e4m3 value is
+// an f16 value).
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t pair16) {
+  uint32_t r;
+  const uint16_t x = (uint16_t)pair16;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(x));
+  return r;
+}
+
+// Byte permute: result byte i = byte (sel >> 4i & 7) of {b:a}.
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+
+// Two 16-bit values of the I/O type (bf16 when BF16) as two f16.
+template <bool BF16>
+__device__ __forceinline__ uint32_t to_f16x2(uint32_t x) {
+  if constexpr (BF16) {
+    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&x));
+    const __half2 h = __float22half2_rn(f);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  } else {
+    return x;
+  }
+}
+
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

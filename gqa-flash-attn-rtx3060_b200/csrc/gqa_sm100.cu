@@ -92,6 +92,10 @@ int init_device(int dev) {
   GQA_SET_STREAM(64, true, 1); GQA_SET_STREAM(64, true, 2); GQA_SET_STREAM(64, true, 4);
   GQA_SET_STREAM(64, false, 1); GQA_SET_STREAM(64, false, 2); GQA_SET_STREAM(64, false, 4);
 #undef GQA_SET_STREAM
+#define GQA_SET_STREAM_F8(BF, RG) chk(set_smem(gqa_stream_kernel<128, BF, RG, true>, StreamCfg<64>::kSmemBytes))
+  GQA_SET_STREAM_F8(true, 1); GQA_SET_STREAM_F8(true, 2); GQA_SET_STREAM_F8(true, 4);
+  GQA_SET_STREAM_F8(false, 1); GQA_SET_STREAM_F8(false, 2); GQA_SET_STREAM_F8(false, 4);
+#undef GQA_SET_STREAM_F8
   if (e != cudaSuccess) return GQA_ERR_CUDA;
   return GQA_OK;
 }
@@ -142,20 +146,23 @@ int check_strides(const void* ptr, const int64_t* st) {
   return GQA_OK;
 }
 
-// 4-D tensor map over a (b, h, s, d) 16-bit tensor, box {64, box_s, box_h, 1}, 128-byte swizzle.
+// 4-D tensor map over a (b, h, s, d) 16-bit tensor (8-bit with `u8`), box {128 bytes of d,
+// box_s, box_h, 1}, 128-byte swizzle. Strides are in elements.
 int make_map(CUtensorMap* map, const void* ptr, const int64_t* st, int b, int h, int s, int d, int box_s,
-             int box_h) {
+             int box_h, bool u8 = false) {
+  const cuuint64_t es = u8 ? 1 : 2;
   cuuint64_t dims[4] = {(cuuint64_t)d, (cuuint64_t)s, (cuuint64_t)h, (cuuint64_t)b};
-  cuuint64_t strides[3] = {(cuuint64_t)st[2] * 2, (cuuint64_t)st[1] * 2, (cuuint64_t)st[0] * 2};
+  cuuint64_t strides[3] = {(cuuint64_t)st[2] * es, (cuuint64_t)st[1] * es, (cuuint64_t)st[0] * es};
   // Degenerate strides (size-1 dims) may be 0 in caller metadata; TMA wants a valid stride.
-  if (s == 1 && strides[0] == 0) strides[0] = (cuuint64_t)d * 2;
+  if (s == 1 && strides[0] == 0) strides[0] = (cuuint64_t)d * es;
   if (h == 1 && strides[1] == 0) strides[1] = strides[0] * s;
   if (b == 1 && strides[2] == 0) strides[2] = strides[1] * h;
   for (int i = 0; i < 3; ++i)
     if (strides[i] == 0 || (strides[i] & 15) != 0 || strides[i] >= (1ull << 40)) return GQA_ERR_ALIGNMENT;
-  cuuint32_t box[4] = {64u, (cuuint32_t)box_s, (cuuint32_t)box_h, 1u};
+  cuuint32_t box[4] = {u8 ? 128u : 64u, (cuuint32_t)box_s, (cuuint32_t)box_h, 1u};
   cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
-  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, const_cast<void*>(ptr), dims, strides, box, estr,
+  CUresult r = g_encode(map, u8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 4,
+                        const_cast<void*>(ptr), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? GQA_OK : GQA_ERR_CUDA;
@@ -313,15 +320,16 @@ void prefill_ws_carve(const PrefillPlan& pl, int head_dim, void* ws, PrefillPara
   (void)head_dim;
 }
 
-template <int HD, bool BF>
+template <int HD, bool BF, bool F8 = false>
 cudaError_t launch_stream_hd(const StreamParams& p, const StreamPlan& pl, const CUtensorMap& km,
                              const CUtensorMap& vm, cudaStream_t st) {
+  using Cfg = StreamCfg<F8 ? 64 : HD>;
   const dim3 grid(pl.units * pl.nsplit);
-  const int smem = StreamCfg<HD>::kSmemBytes;
+  const int smem = Cfg::kSmemBytes;
   switch (pl.rg) {
-    case 1: return launch_pdl(gqa_stream_kernel<HD, BF, 1>, grid, StreamCfg<HD>::kThreads, smem, st, p, km, vm);
-    case 2: return launch_pdl(gqa_stream_kernel<HD, BF, 2>, grid, StreamCfg<HD>::kThreads, smem, st, p, km, vm);
-    default: return launch_pdl(gqa_stream_kernel<HD, BF, 4>, grid, StreamCfg<HD>::kThreads, smem, st, p, km, vm);
+    case 1: return launch_pdl(gqa_stream_kernel<HD, BF, 1, F8>, grid, Cfg::kThreads, smem, st, p, km, vm);
+    case 2: return launch_pdl(gqa_stream_kernel<HD, BF, 2, F8>, grid, Cfg::kThreads, smem, st, p, km, vm);
+    default: return launch_pdl(gqa_stream_kernel<HD, BF, 4, F8>, grid, Cfg::kThreads, smem, st, p, km, vm);
   }
 }
 
@@ -330,6 +338,7 @@ cudaError_t launch_stream_hd(const StreamParams& p, const StreamPlan& pl, const 
 // num_blocks) with {64, 1, 64, 1} boxes: the same 64-key x 128-byte smem tiles.
 struct PagedCache {
   int block_size, num_blocks;
+  bool fp8 = false;  // e4m3 K/V (head_dim 128)
 };
 
 int run_stream(const Shape& s, const StreamPlan& pl, StreamParams p, const void* k, const void* v,
@@ -339,8 +348,8 @@ int run_stream(const Shape& s, const StreamPlan& pl, StreamParams p, const void*
   if (paged) {
     const int64_t cs[4] = {(int64_t)paged->block_size * s.hkv * s.head_dim, (int64_t)s.hkv * s.head_dim,
                            s.head_dim, 1};
-    rc = make_map(&km, k, cs, paged->num_blocks, paged->block_size, s.hkv, s.head_dim, 1, 64);
-    if (!rc) rc = make_map(&vm, v, cs, paged->num_blocks, paged->block_size, s.hkv, s.head_dim, 1, 64);
+    rc = make_map(&km, k, cs, paged->num_blocks, paged->block_size, s.hkv, s.head_dim, 1, 64, paged->fp8);
+    if (!rc) rc = make_map(&vm, v, cs, paged->num_blocks, paged->block_size, s.hkv, s.head_dim, 1, 64, paged->fp8);
   } else {
     rc = make_map(&km, k, ks, s.batch, s.hkv, s.seq_kv, s.head_dim, 64, 1);
     if (!rc) rc = make_map(&vm, v, vs, s.batch, s.hkv, s.seq_kv, s.head_dim, 64, 1);
@@ -359,7 +368,9 @@ int run_stream(const Shape& s, const StreamPlan& pl, StreamParams p, const void*
   p.chunk = pl.chunk;
   cudaError_t e;
   const bool bf = dtype == GQA_DTYPE_BF16;
-  if (s.head_dim == 128)
+  if (paged && paged->fp8)
+    e = bf ? launch_stream_hd<128, true, true>(p, pl, km, vm, st) : launch_stream_hd<128, false, true>(p, pl, km, vm, st);
+  else if (s.head_dim == 128)
     e = bf ? launch_stream_hd<128, true>(p, pl, km, vm, st) : launch_stream_hd<128, false>(p, pl, km, vm, st);
   else
     e = bf ? launch_stream_hd<64, true>(p, pl, km, vm, st) : launch_stream_hd<64, false>(p, pl, km, vm, st);
@@ -463,6 +474,74 @@ int check_common(const void* q, const void* k, const void* v, const int64_t* qs,
   return rc;
 }
 
+// Paged forward over 16-bit or (fp8) e4m3 caches; the C ABI's gqa_paged_fwd and
+// gqa_paged_fwd_kv8.
+int paged_forward(const void* q, const void* k_cache, const void* v_cache, void* o, const int64_t* qs,
+                  const int64_t* os, const int* block_table, int bt_stride, const int* seq_lens, int num_seqs,
+                  int num_heads, int num_kv_heads, int seq_q, int head_dim, int block_size, int num_blocks,
+                  int max_seq_len, float scale_log2, int causal, int dtype, void* workspace, size_t workspace_bytes,
+                  void* stream, bool fp8, float k_scale, float v_scale) {
+  Shape s;
+  int rc = check_shape(num_seqs, num_heads, num_kv_heads, seq_q, max_seq_len, head_dim, &s);
+  if (rc) return rc;
+  if (!qs || !os) return GQA_ERR_INVALID_ARG;
+  if (num_seqs == 0 || seq_q == 0) return GQA_OK;
+  if (dtype != GQA_DTYPE_BF16 && dtype != GQA_DTYPE_F16) return GQA_ERR_UNSUPPORTED;
+  if (block_size < 64 || (block_size & (block_size - 1)) != 0 || num_blocks <= 0) return GQA_ERR_UNSUPPORTED;
+  // fp8 K/V: the streaming kernel only (decode and short chunks), rows of 128 e4m3 values.
+  if (fp8 && (head_dim != 128 || !use_stream(s))) return GQA_ERR_UNSUPPORTED;
+  if (fp8 && !(k_scale > 0.f && v_scale > 0.f)) return GQA_ERR_INVALID_ARG;
+  if (!k_cache || !v_cache || !block_table || !seq_lens || bt_stride <= 0) return GQA_ERR_INVALID_ARG;
+  if (max_seq_len > (int64_t)bt_stride * block_size) return GQA_ERR_INVALID_ARG;
+  if (!aligned16(k_cache) || !aligned16(v_cache)) return GQA_ERR_ALIGNMENT;
+  rc = check_strides(q, qs);
+  if (!rc) rc = check_strides(o, os);
+  if (rc) return rc;
+  int sm = 0;
+  rc = current_device(&sm);
+  if (rc) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (max_seq_len == 0) return fill_nan(o, os, s, dtype, st);
+  int shift = 0;
+  while ((1 << shift) < block_size) ++shift;
+  const PagedCache pc{block_size, num_blocks, fp8};
+
+  if (use_stream(s)) {  // decode and short chunks: the streaming kernel
+    StreamPlan pl = plan_stream(s, sm, true);
+    StreamParams p{};
+    p.q = reinterpret_cast<const uint16_t*>(q);
+    p.o = o;
+    p.q_sb = qs[0]; p.q_sh = qs[1]; p.q_sm = qs[2];
+    p.o_sb = os[0]; p.o_sh = os[1]; p.o_sm = os[2];
+    p.causal = causal ? 1 : 0;
+    p.scale_log2 = fp8 ? scale_log2 * k_scale : scale_log2;
+    p.v_scale = fp8 ? v_scale : 1.0f;
+    p.kv_offset = 0;
+    p.seq_kv_total = max_seq_len;
+    p.block_table = block_table;
+    p.seq_lens = seq_lens;
+    p.bt_stride = bt_stride;
+    p.block_shift = shift;
+    if (pl.nsplit > 1 && workspace && workspace_bytes >= stream_ws_bytes(pl, head_dim)) {
+      p.mode = kStreamFused;
+      stream_ws_carve(pl, head_dim, workspace, &p);
+    } else {
+      pl = plan_stream(s, sm, false);
+      p.mode = kStreamOut;
+    }
+    return run_stream(s, pl, p, k_cache, v_cache, nullptr, nullptr, dtype, st, &pc);
+  }
+
+  PrefillParams p{};  // longer chunks: the tcgen05 prefill kernel over the paged cache
+  p.block_table = block_table;
+  p.seq_lens = seq_lens;
+  p.bt_stride = bt_stride;
+  p.block_shift = shift;
+  p.num_blocks = num_blocks;
+  return run_prefill(s, plan_prefill(s, sm, causal != 0), q, k_cache, v_cache, o, qs, nullptr, nullptr, os,
+                     scale_log2, causal, dtype, workspace, workspace_bytes, st, &pc, p);
+}
+
 }  // namespace
 }  // namespace gqa
 
@@ -474,8 +553,9 @@ const char* gqa_strerror(int code) {
   switch (code) {
     case GQA_OK: return "success";
     case GQA_ERR_INVALID_ARG: return "invalid argument (shape, null pointer or negative size)";
-    case GQA_ERR_UNSUPPORTED: return "unsupported configuration (head_dim must be 64 or 128, dtype f16/bf16, "
-                                     "num_heads/num_kv_heads a power of two <= 128)";
+    case GQA_ERR_UNSUPPORTED: return "unsupported configuration (head_dim 64 or 128, dtype f16/bf16, "
+                                     "num_heads/num_kv_heads a power of two <= 128; paged: block_size a power "
+                                     "of two >= 64; fp8 K/V: head_dim 128 and group * seq_q <= 64)";
     case GQA_ERR_ALIGNMENT: return "tensor must be contiguous in head_dim with 16-byte aligned base and strides";
     case GQA_ERR_CUDA: return "CUDA runtime or driver call failed";
     case GQA_ERR_TIMEOUT: return "bounded in-kernel wait expired (kernel aborted)";
@@ -523,61 +603,19 @@ int gqa_paged_fwd(const void* q, const void* k_cache, const void* v_cache, void*
                   int num_heads, int num_kv_heads, int seq_q, int head_dim, int block_size, int num_blocks,
                   int max_seq_len, float scale_log2, int causal, int dtype, void* workspace, size_t workspace_bytes,
                   void* stream) {
-  Shape s;
-  int rc = check_shape(num_seqs, num_heads, num_kv_heads, seq_q, max_seq_len, head_dim, &s);
-  if (rc) return rc;
-  if (!qs || !os) return GQA_ERR_INVALID_ARG;
-  if (num_seqs == 0 || seq_q == 0) return GQA_OK;
-  if (dtype != GQA_DTYPE_BF16 && dtype != GQA_DTYPE_F16) return GQA_ERR_UNSUPPORTED;
-  if (block_size < 64 || (block_size & (block_size - 1)) != 0 || num_blocks <= 0) return GQA_ERR_UNSUPPORTED;
-  if (!k_cache || !v_cache || !block_table || !seq_lens || bt_stride <= 0) return GQA_ERR_INVALID_ARG;
-  if (max_seq_len > (int64_t)bt_stride * block_size) return GQA_ERR_INVALID_ARG;
-  if (!aligned16(k_cache) || !aligned16(v_cache)) return GQA_ERR_ALIGNMENT;
-  rc = check_strides(q, qs);
-  if (!rc) rc = check_strides(o, os);
-  if (rc) return rc;
-  int sm = 0;
-  rc = current_device(&sm);
-  if (rc) return rc;
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (max_seq_len == 0) return fill_nan(o, os, s, dtype, st);
-  int shift = 0;
-  while ((1 << shift) < block_size) ++shift;
-  const PagedCache pc{block_size, num_blocks};
+  return gqa::paged_forward(q, k_cache, v_cache, o, qs, os, block_table, bt_stride, seq_lens, num_seqs, num_heads,
+                            num_kv_heads, seq_q, head_dim, block_size, num_blocks, max_seq_len, scale_log2, causal,
+                            dtype, workspace, workspace_bytes, stream, false, 1.0f, 1.0f);
+}
 
-  if (use_stream(s)) {  // decode and short chunks: the streaming kernel
-    StreamPlan pl = plan_stream(s, sm, true);
-    StreamParams p{};
-    p.q = reinterpret_cast<const uint16_t*>(q);
-    p.o = o;
-    p.q_sb = qs[0]; p.q_sh = qs[1]; p.q_sm = qs[2];
-    p.o_sb = os[0]; p.o_sh = os[1]; p.o_sm = os[2];
-    p.causal = causal ? 1 : 0;
-    p.scale_log2 = scale_log2;
-    p.kv_offset = 0;
-    p.seq_kv_total = max_seq_len;
-    p.block_table = block_table;
-    p.seq_lens = seq_lens;
-    p.bt_stride = bt_stride;
-    p.block_shift = shift;
-    if (pl.nsplit > 1 && workspace && workspace_bytes >= stream_ws_bytes(pl, head_dim)) {
-      p.mode = kStreamFused;
-      stream_ws_carve(pl, head_dim, workspace, &p);
-    } else {
-      pl = plan_stream(s, sm, false);
-      p.mode = kStreamOut;
-    }
-    return run_stream(s, pl, p, k_cache, v_cache, nullptr, nullptr, dtype, st, &pc);
-  }
-
-  PrefillParams p{};  // longer chunks: the tcgen05 prefill kernel over the paged cache
-  p.block_table = block_table;
-  p.seq_lens = seq_lens;
-  p.bt_stride = bt_stride;
-  p.block_shift = shift;
-  p.num_blocks = num_blocks;
-  return run_prefill(s, plan_prefill(s, sm, causal != 0), q, k_cache, v_cache, o, qs, nullptr, nullptr, os,
-                     scale_log2, causal, dtype, workspace, workspace_bytes, st, &pc, p);
+int gqa_paged_fwd_kv8(const void* q, const void* k_cache, const void* v_cache, void* o, const int64_t* qs,
+                      const int64_t* os, const int* block_table, int bt_stride, const int* seq_lens, int num_seqs,
+                      int num_heads, int num_kv_heads, int seq_q, int head_dim, int block_size, int num_blocks,
+                      int max_seq_len, float scale_log2, float k_scale, float v_scale, int causal, int dtype,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+  return gqa::paged_forward(q, k_cache, v_cache, o, qs, os, block_table, bt_stride, seq_lens, num_seqs, num_heads,
+                            num_kv_heads, seq_q, head_dim, block_size, num_blocks, max_seq_len, scale_log2, causal,
+                            dtype, workspace, workspace_bytes, stream, true, k_scale, v_scale);
 }
 
 size_t gqa_fwd_workspace_bytes(int batch, int num_heads, int num_kv_heads, int seq_q, int seq_kv, int head_dim) {

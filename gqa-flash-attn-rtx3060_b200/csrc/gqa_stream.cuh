@@ -66,6 +66,9 @@ struct StreamParams {
   const int* seq_lens;
   int bt_stride;
   int block_shift;
+  // fp8 K/V (the FP8 instantiation): stored value x scale = real value. k_scale is
+  // folded into scale_log2 by the host; v_scale multiplies the accumulators once.
+  float v_scale;
 };
 
 template <int HD>
@@ -88,11 +91,17 @@ struct StreamCfg {
 
 #define GQA_CBAR() asm volatile("bar.sync 1, 256;" ::: "memory")  // the 8 compute warps
 
-template <int HD, bool BF16, int RG>
+// FP8: K and V are e4m3 (HD = 128, so a key row is 128 bytes, the shared-memory
+// geometry of a 16-bit HD = 64 row); Q and O keep the 16-bit I/O type. Both MMAs
+// then run in f16: Q is converted once, K and V fragments are converted exactly
+// from e4m3 after ldmatrix, and P is packed as f16 (P <= 1).
+template <int HD, bool BF16, int RG, bool FP8 = false>
 __global__ void __launch_bounds__(288, 1)
     gqa_stream_kernel(const StreamParams p, const __grid_constant__ CUtensorMap kmap,
                       const __grid_constant__ CUtensorMap vmap) {
-  using Cfg = StreamCfg<HD>;
+  static_assert(!FP8 || HD == 128, "fp8 K/V rows are 128 bytes");
+  using Cfg = StreamCfg<FP8 ? 64 : HD>;  // ring geometry (bytes per key row)
+  constexpr bool MMA_BF16 = BF16 && !FP8;  // operand type of both MMAs
   constexpr int NW = Cfg::kWarps;
   constexpr int KS = NW / RG;           // warps sharing one row group split the stage's keys
   constexpr int NKW = Cfg::kBN / KS;    // keys per warp per stage (16, 32, 64)
@@ -249,13 +258,29 @@ __global__ void __launch_bounds__(288, 1)
 
   // Q fragments (A operand, 16 rows x HD), loaded once.
   uint32_t qa[NKS][4];
+  if constexpr (FP8) {
+    // k16 step kk covers d 16kk..16kk+15 in the order the e4m3 K fragments take
+    // (k 2t, 2t+1 -> d 4t, 4t+1; k 2t+8, 2t+9 -> d 4t+2, 4t+3), in f16.
 #pragma unroll
-  for (int kk = 0; kk < NKS; ++kk) {
-    const int d0 = kk * 16 + gc * 2;
-    qa[kk][0] = qrow[0] ? *reinterpret_cast<const uint32_t*>(qrow[0] + d0) : 0u;
-    qa[kk][1] = qrow[1] ? *reinterpret_cast<const uint32_t*>(qrow[1] + d0) : 0u;
-    qa[kk][2] = qrow[0] ? *reinterpret_cast<const uint32_t*>(qrow[0] + d0 + 8) : 0u;
-    qa[kk][3] = qrow[1] ? *reinterpret_cast<const uint32_t*>(qrow[1] + d0 + 8) : 0u;
+    for (int kk = 0; kk < NKS; ++kk) {
+      const int d0 = kk * 16 + gc * 4;
+      const uint2 z = make_uint2(0u, 0u);
+      const uint2 q0 = qrow[0] ? *reinterpret_cast<const uint2*>(qrow[0] + d0) : z;
+      const uint2 q1 = qrow[1] ? *reinterpret_cast<const uint2*>(qrow[1] + d0) : z;
+      qa[kk][0] = to_f16x2<BF16>(q0.x);
+      qa[kk][1] = to_f16x2<BF16>(q1.x);
+      qa[kk][2] = to_f16x2<BF16>(q0.y);
+      qa[kk][3] = to_f16x2<BF16>(q1.y);
+    }
+  } else {
+#pragma unroll
+    for (int kk = 0; kk < NKS; ++kk) {
+      const int d0 = kk * 16 + gc * 2;
+      qa[kk][0] = qrow[0] ? *reinterpret_cast<const uint32_t*>(qrow[0] + d0) : 0u;
+      qa[kk][1] = qrow[1] ? *reinterpret_cast<const uint32_t*>(qrow[1] + d0) : 0u;
+      qa[kk][2] = qrow[0] ? *reinterpret_cast<const uint32_t*>(qrow[0] + d0 + 8) : 0u;
+      qa[kk][3] = qrow[1] ? *reinterpret_cast<const uint32_t*>(qrow[1] + d0 + 8) : 0u;
+    }
   }
 
   float acc[NDB][4];
@@ -278,17 +303,36 @@ __global__ void __launch_bounds__(288, 1)
       float s[NNB][4];
 #pragma unroll
       for (int nb = 0; nb < NNB; ++nb) s[nb][0] = s[nb][1] = s[nb][2] = s[nb][3] = 0.f;
+      if constexpr (FP8) {
+        // A 16-byte chunk of a key row is 16 e4m3 values of d, one k16 step: lane
+        // (g, t) of an 8 x 16-byte ldmatrix gets d 4t..4t+3 of key g, i.e. both B
+        // registers of the step in the order the Q fragments were loaded in.
 #pragma unroll
-      for (int kc = 0; kc < HD / 32; ++kc) {
+        for (int kc = 0; kc < HD / 64; ++kc) {
 #pragma unroll
-        for (int nb = 0; nb < NNB; ++nb) {
-          const int krow = ks * NKW + nb * 8 + (lane & 7);
-          const int chunk = kc * 4 + (lane >> 3);
-          const uint32_t addr = kst + (chunk >> 3) * Cfg::kSubBytes + sw128_off(krow, chunk & 7);
-          uint32_t b0, b1, b2, b3;
-          ldsm_x4(addr, b0, b1, b2, b3);
-          mma_16816<BF16>(s[nb], qa[2 * kc], b0, b1);
-          mma_16816<BF16>(s[nb], qa[2 * kc + 1], b2, b3);
+          for (int nb = 0; nb < NNB; ++nb) {
+            const int krow = ks * NKW + nb * 8 + (lane & 7);
+            const int chunk = kc * 4 + (lane >> 3);
+            uint32_t r[4];
+            ldsm_x4(kst + sw128_off(krow, chunk), r[0], r[1], r[2], r[3]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              mma_16816<false>(s[nb], qa[4 * kc + j], e4m3x2_to_f16x2(r[j]), e4m3x2_to_f16x2(r[j] >> 16));
+          }
+        }
+      } else {
+#pragma unroll
+        for (int kc = 0; kc < HD / 32; ++kc) {
+#pragma unroll
+          for (int nb = 0; nb < NNB; ++nb) {
+            const int krow = ks * NKW + nb * 8 + (lane & 7);
+            const int chunk = kc * 4 + (lane >> 3);
+            const uint32_t addr = kst + (chunk >> 3) * Cfg::kSubBytes + sw128_off(krow, chunk & 7);
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4(addr, b0, b1, b2, b3);
+            mma_16816<BF16>(s[nb], qa[2 * kc], b0, b1);
+            mma_16816<BF16>(s[nb], qa[2 * kc + 1], b2, b3);
+          }
         }
       }
 
@@ -339,19 +383,39 @@ __global__ void __launch_bounds__(288, 1)
 #pragma unroll
       for (int kk = 0; kk < NKW / 16; ++kk) {
         uint32_t pa[4];
-        pa[0] = pack2<BF16>(s[2 * kk][0], s[2 * kk][1]);
-        pa[1] = pack2<BF16>(s[2 * kk][2], s[2 * kk][3]);
-        pa[2] = pack2<BF16>(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-        pa[3] = pack2<BF16>(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+        pa[0] = pack2<MMA_BF16>(s[2 * kk][0], s[2 * kk][1]);
+        pa[1] = pack2<MMA_BF16>(s[2 * kk][2], s[2 * kk][3]);
+        pa[2] = pack2<MMA_BF16>(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+        pa[3] = pack2<MMA_BF16>(s[2 * kk + 1][2], s[2 * kk + 1][3]);
         const int vrow = ks * NKW + kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        if constexpr (FP8) {
+          // Transposed 8 x 16-byte loads of keys 0-7 and 8-15 of 16-d chunks c, c+1:
+          // lane (g, t) gets keys 2t, 2t+1 x d 2g, 2g+1 of each. Bytes (0, 2) are the
+          // B pair of column d = 2g, bytes (1, 3) that of d = 2g + 1, so chunk c
+          // feeds accumulator blocks 2c (even d) and 2c + 1 (odd d).
 #pragma unroll
-        for (int dc = 0; dc < NDB; dc += 2) {
-          const int chunk = dc + (lane >> 4);
-          const uint32_t addr = vst + (chunk >> 3) * Cfg::kSubBytes + sw128_off(vrow, chunk & 7);
-          uint32_t b0, b1, b2, b3;
-          ldsm_x4_t(addr, b0, b1, b2, b3);
-          mma_16816<BF16>(acc[dc], pa, b0, b1);
-          mma_16816<BF16>(acc[dc + 1], pa, b2, b3);
+          for (int c = 0; c < HD / 16; c += 2) {
+            const int chunk = c + (lane >> 4);
+            uint32_t r[4];
+            ldsm_x4_t(vst + sw128_off(vrow, chunk), r[0], r[1], r[2], r[3]);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const uint32_t lo = prmt(r[2 * h], 0u, 0x3120u);      // keys 0-7:  even pair | odd pair
+              const uint32_t hi = prmt(r[2 * h + 1], 0u, 0x3120u);  // keys 8-15
+              mma_16816<false>(acc[2 * (c + h)], pa, e4m3x2_to_f16x2(lo), e4m3x2_to_f16x2(hi));
+              mma_16816<false>(acc[2 * (c + h) + 1], pa, e4m3x2_to_f16x2(lo >> 16), e4m3x2_to_f16x2(hi >> 16));
+            }
+          }
+        } else {
+#pragma unroll
+          for (int dc = 0; dc < NDB; dc += 2) {
+            const int chunk = dc + (lane >> 4);
+            const uint32_t addr = vst + (chunk >> 3) * Cfg::kSubBytes + sw128_off(vrow, chunk & 7);
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4_t(addr, b0, b1, b2, b3);
+            mma_16816<BF16>(acc[dc], pa, b0, b1);
+            mma_16816<BF16>(acc[dc + 1], pa, b2, b3);
+          }
         }
       }
     }
@@ -379,11 +443,26 @@ __global__ void __launch_bounds__(288, 1)
   {
     float* aw = abuf + warp * 16 * AS;
     const bool upper = rg * 16 + 8 < p.rows;  // warp-uniform
+    if constexpr (FP8) {
+      // Blocks 2c, 2c + 1 hold d = 16c + 4t + {0, 2} and {1, 3}: four consecutive d.
+      const float vs = p.v_scale;
 #pragma unroll
-    for (int i = 0; i < NDB; ++i) {
-      const int d = i * 8 + gc * 2;
-      *reinterpret_cast<float2*>(aw + gr * AS + d) = make_float2(acc[i][0], acc[i][1]);
-      if (upper) *reinterpret_cast<float2*>(aw + (gr + 8) * AS + d) = make_float2(acc[i][2], acc[i][3]);
+      for (int c = 0; c < HD / 16; ++c) {
+        const int d = c * 16 + gc * 4;
+        const float* e = acc[2 * c];
+        const float* o = acc[2 * c + 1];
+        *reinterpret_cast<float4*>(aw + gr * AS + d) = make_float4(e[0] * vs, o[0] * vs, e[1] * vs, o[1] * vs);
+        if (upper)
+          *reinterpret_cast<float4*>(aw + (gr + 8) * AS + d) =
+              make_float4(e[2] * vs, o[2] * vs, e[3] * vs, o[3] * vs);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < NDB; ++i) {
+        const int d = i * 8 + gc * 2;
+        *reinterpret_cast<float2*>(aw + gr * AS + d) = make_float2(acc[i][0], acc[i][1]);
+        if (upper) *reinterpret_cast<float2*>(aw + (gr + 8) * AS + d) = make_float2(acc[i][2], acc[i][3]);
+      }
     }
     if (gc == 0) {
       mbuf[warp * 16 + gr] = m_run[0];

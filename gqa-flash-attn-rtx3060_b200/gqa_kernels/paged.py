@@ -28,13 +28,15 @@ __all__ = ["paged_decode", "paged_prefill"]
 LOG2E = 1.4426950408889634
 
 
-def paged_decode(query, key_cache, value_cache, block_tables, seq_lens, max_seq_len=None, scale=None):
+def paged_decode(query, key_cache, value_cache, block_tables, seq_lens, max_seq_len=None, scale=None,
+                 k_scale=1.0, v_scale=1.0):
     """Decode attention over a paged K/V cache.
 
     Args:
         query: (num_seqs, num_heads, head_dim), bf16 or fp16, one token per sequence.
         key_cache, value_cache: (num_blocks, block_size, num_kv_heads, head_dim), contiguous,
-            block_size a power of two >= 64.
+            block_size a power of two >= 64; query's dtype, or torch.float8_e4m3fn (head_dim
+            128) with key = stored key * k_scale and value = stored value * v_scale.
         block_tables: int32 (num_seqs, max_blocks_per_seq); sequence b's key k is in block
             block_tables[b, k // block_size] at position k % block_size.
         seq_lens: int32 (num_seqs,), keys cached per sequence (the new token's included).
@@ -45,6 +47,9 @@ def paged_decode(query, key_cache, value_cache, block_tables, seq_lens, max_seq_
     Returns:
         (num_seqs, num_heads, head_dim), query's dtype. Asynchronous on the current stream.
     """
+    if key_cache.dtype == torch.float8_e4m3fn:  # one query position: the chunked entry point
+        return paged_prefill(query.unsqueeze(2), key_cache, value_cache, block_tables, seq_lens, max_seq_len,
+                             scale, causal=False, k_scale=k_scale, v_scale=v_scale)[:, :, 0]
     num_seqs, num_heads, head_dim = query.shape
     num_blocks, block_size, num_kv_heads = _check_cache(query, key_cache, value_cache, block_tables, seq_lens,
                                                         num_seqs, num_heads, head_dim)
@@ -83,8 +88,8 @@ def _check_cache(query, key_cache, value_cache, block_tables, seq_lens, num_seqs
         raise ValueError("num_heads must be divisible by num_kv_heads")
     if not (query.is_cuda and key_cache.is_cuda and value_cache.is_cuda):
         raise ValueError("tensors must be on a CUDA device")
-    if not (query.dtype == key_cache.dtype == value_cache.dtype):
-        raise TypeError("query and the caches must share one dtype")
+    if key_cache.dtype != value_cache.dtype or key_cache.dtype not in (query.dtype, torch.float8_e4m3fn):
+        raise TypeError("the caches must share query's dtype, or both be float8_e4m3fn")
     if not (key_cache.is_contiguous() and value_cache.is_contiguous()):
         raise ValueError("the caches must be contiguous")
     if block_tables.dtype != torch.int32 or seq_lens.dtype != torch.int32:
@@ -95,7 +100,7 @@ def _check_cache(query, key_cache, value_cache, block_tables, seq_lens, num_seqs
 
 
 def paged_prefill(query, key_cache, value_cache, block_tables, seq_lens, max_seq_len=None, scale=None,
-                  causal=True):
+                  causal=True, k_scale=1.0, v_scale=1.0):
     """Attention of a chunk of new tokens per sequence over a paged K/V cache.
 
     Args:
@@ -104,7 +109,9 @@ def paged_prefill(query, key_cache, value_cache, block_tables, seq_lens, max_seq
             chunk_len positions of each sequence, whose keys (the chunk's own included)
             are already in the cache.
         key_cache, value_cache: (num_blocks, block_size, num_kv_heads, head_dim), contiguous,
-            block_size a power of two >= 64.
+            block_size a power of two >= 64; query's dtype, or torch.float8_e4m3fn with
+            key = stored key * k_scale and value = stored value * v_scale (head_dim 128 and
+            group * chunk_len <= 64: the streaming kernel).
         block_tables: int32 (num_seqs, max_blocks_per_seq); sequence b's key k is in block
             block_tables[b, k // block_size] at position k % block_size.
         seq_lens: int32 (num_seqs,), keys cached per sequence (the chunk included).
@@ -135,15 +142,21 @@ def paged_prefill(query, key_cache, value_cache, block_tables, seq_lens, max_seq
                                                      head_dim)
         ws = _lib.WORKSPACES.get(query.device, ws_bytes,
                                  ("paged_fwd", num_seqs, num_heads, num_kv_heads, chunk_len, max_seq_len, head_dim))
-        rc = lib.gqa_paged_fwd(
-            ctypes.c_void_p(query.data_ptr()), ctypes.c_void_p(key_cache.data_ptr()),
-            ctypes.c_void_p(value_cache.data_ptr()), ctypes.c_void_p(out.data_ptr()),
-            _lib.strides(query), _lib.strides(out),
-            ctypes.c_void_p(block_tables.data_ptr()), block_tables.stride(0), ctypes.c_void_p(seq_lens.data_ptr()),
-            num_seqs, num_heads, num_kv_heads, chunk_len, head_dim, block_size, num_blocks, max_seq_len,
-            float(scale * LOG2E), 1 if causal else 0, _lib.dtype_code(query),
-            ctypes.c_void_p(ws.data_ptr()), ctypes.c_size_t(ws.numel()), _lib.stream_ptr(query.device))
+        fp8 = key_cache.dtype == torch.float8_e4m3fn
+        common = (ctypes.c_void_p(query.data_ptr()), ctypes.c_void_p(key_cache.data_ptr()),
+                  ctypes.c_void_p(value_cache.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+                  _lib.strides(query), _lib.strides(out),
+                  ctypes.c_void_p(block_tables.data_ptr()), block_tables.stride(0),
+                  ctypes.c_void_p(seq_lens.data_ptr()),
+                  num_seqs, num_heads, num_kv_heads, chunk_len, head_dim, block_size, num_blocks, max_seq_len,
+                  float(scale * LOG2E))
+        tail = (1 if causal else 0, _lib.dtype_code(query), ctypes.c_void_p(ws.data_ptr()),
+                ctypes.c_size_t(ws.numel()), _lib.stream_ptr(query.device))
+        if fp8:
+            rc = lib.gqa_paged_fwd_kv8(*common, float(k_scale), float(v_scale), *tail)
+        else:
+            rc = lib.gqa_paged_fwd(*common, *tail)
         if rc != 0:
             _lib.WORKSPACES.drop(query.device)
-        _lib.check(rc, "gqa_paged_fwd")
+        _lib.check(rc, "gqa_paged_fwd_kv8" if fp8 else "gqa_paged_fwd")
     return out

@@ -212,6 +212,24 @@ int gqa_paged_fwd(const void* q, const void* k_cache, const void* v_cache, void*
                   size_t workspace_bytes, void* stream);
 
 /*
+ * gqa_paged_fwd over fp8 caches: k_cache/v_cache hold e4m3 values (one byte
+ * each, same layout), and key = stored key x k_scale, value = stored value x
+ * v_scale (vLLM's fp8 KV-cache convention; both scales > 0). q/o keep `dtype`
+ * (bf16 or fp16). head_dim must be 128 and group * seq_q <= 64 (decode and
+ * short chunks: the streaming kernel, whose K/V fragments are converted exactly
+ * from e4m3 to f16 in registers; both MMAs run in f16, so |q| must stay within
+ * the f16 range). Otherwise GQA_ERR_UNSUPPORTED. The workspace is
+ * gqa_paged_fwd_workspace_bytes(). Halves the bytes streamed per key against
+ * 16-bit caches.
+ * No reference counterpart: the reference's K/V are bf16 or fp16 only.
+ */
+int gqa_paged_fwd_kv8(const void* q, const void* k_cache, const void* v_cache, void* o, const int64_t* q_strides,
+                      const int64_t* o_strides, const int* block_table, int bt_stride, const int* seq_lens,
+                      int num_seqs, int num_heads, int num_kv_heads, int seq_q, int head_dim, int block_size,
+                      int num_blocks, int max_seq_len, float scale_log2, float k_scale, float v_scale, int causal,
+                      int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Reads (and clears, if `clear` is nonzero) the device error word of the
  * current device: 0, or GQA_ERR_TIMEOUT when a bounded in-kernel wait expired.
  * `site` (optional) receives the wait site id. Synchronises the current device.
