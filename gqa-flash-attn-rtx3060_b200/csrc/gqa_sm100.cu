@@ -618,6 +618,21 @@ int gqa_paged_fwd_kv8(const void* q, const void* k_cache, const void* v_cache, v
                             dtype, workspace, workspace_bytes, stream, true, k_scale, v_scale);
 }
 
+int gqa_prefill_plan(int batch, int num_heads, int num_kv_heads, int seq_q, int seq_kv, int head_dim, int causal,
+                     int sm_count, int* plan) {
+  Shape s;
+  const int rc = check_shape(batch, num_heads, num_kv_heads, seq_q, seq_kv, head_dim, &s);
+  if (rc) return rc;
+  if (!plan || sm_count <= 0) return GQA_ERR_INVALID_ARG;
+  const PrefillPlan pl = plan_prefill(s, sm_count, causal != 0);
+  plan[0] = pl.units;
+  plan[1] = pl.nsplit;
+  plan[2] = pl.chunk_tiles;
+  plan[3] = pl.head_major;
+  plan[4] = pl.units * pl.nsplit;
+  return GQA_OK;
+}
+
 size_t gqa_fwd_workspace_bytes(int batch, int num_heads, int num_kv_heads, int seq_q, int seq_kv, int head_dim) {
   Shape s;
   if (check_shape(batch, num_heads, num_kv_heads, seq_q, seq_kv, head_dim, &s)) return 0;

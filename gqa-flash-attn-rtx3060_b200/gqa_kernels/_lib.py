@@ -53,6 +53,7 @@ SIGNATURES = {
     "gqa_paged_fwd_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I, _I]),
     "gqa_paged_fwd": (_I, [_P, _P, _P, _P, _I64P, _I64P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _I, _I,
                            _P, _SZ, _P]),
+    "gqa_prefill_plan": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, ctypes.POINTER(ctypes.c_int)]),
     "gqa_paged_fwd_kv8": (_I, [_P, _P, _P, _P, _I64P, _I64P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _F,
                                _F, _I, _I, _P, _SZ, _P]),
 }

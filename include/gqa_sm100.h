@@ -230,6 +230,16 @@ int gqa_paged_fwd_kv8(const void* q, const void* k_cache, const void* v_cache, v
                       int dtype, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * The tcgen05 prefill path's launch plan for a shape on `sm_count` SMs, without
+ * launching (host only; needs no GPU). plan[0..4] = units (query pairs x batch x
+ * kv heads), nsplit (CTAs per unit; > 1 when the units are fewer than the SMs),
+ * key tiles per split, head-major unit order (0/1), grid size.
+ * No reference counterpart (the reference launches one program per query block).
+ */
+int gqa_prefill_plan(int batch, int num_heads, int num_kv_heads, int seq_q, int seq_kv, int head_dim, int causal,
+                     int sm_count, int* plan);
+
+/*
  * Reads (and clears, if `clear` is nonzero) the device error word of the
  * current device: 0, or GQA_ERR_TIMEOUT when a bounded in-kernel wait expired.
  * `site` (optional) receives the wait site id. Synchronises the current device.
