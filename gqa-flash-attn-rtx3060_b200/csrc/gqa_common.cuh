@@ -345,6 +345,14 @@ __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t pair16) {
   return r;
 }
 
+// Transpose of an 8 x 8 matrix of 16-bit values held one row pair per lane in the
+// mma fragment layout (lane 4g + t holds row g, columns 2t, 2t + 1).
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+  uint32_t r;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(r) : "r"(x));
+  return r;
+}
+
 // Byte permute: result byte i = byte (sel >> 4i & 7) of {b:a}.
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t r;

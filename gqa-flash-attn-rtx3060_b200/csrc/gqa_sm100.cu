@@ -96,6 +96,13 @@ int init_device(int dev) {
   GQA_SET_STREAM_F8(true, 1); GQA_SET_STREAM_F8(true, 2); GQA_SET_STREAM_F8(true, 4);
   GQA_SET_STREAM_F8(false, 1); GQA_SET_STREAM_F8(false, 2); GQA_SET_STREAM_F8(false, 4);
 #undef GQA_SET_STREAM_F8
+  // The transposed (keys x rows) decode instantiations.
+  chk(set_smem(gqa_stream_kernel<128, true, 1, true, true>, StreamCfg<64>::kSmemBytes));
+  chk(set_smem(gqa_stream_kernel<128, false, 1, true, true>, StreamCfg<64>::kSmemBytes));
+  chk(set_smem(gqa_stream_kernel<128, true, 1, false, true>, StreamCfg<128>::kSmemBytes));
+  chk(set_smem(gqa_stream_kernel<128, false, 1, false, true>, StreamCfg<128>::kSmemBytes));
+  chk(set_smem(gqa_stream_kernel<64, true, 1, false, true>, StreamCfg<64>::kSmemBytes));
+  chk(set_smem(gqa_stream_kernel<64, false, 1, false, true>, StreamCfg<64>::kSmemBytes));
   if (e != cudaSuccess) return GQA_ERR_CUDA;
   return GQA_OK;
 }
@@ -326,6 +333,8 @@ cudaError_t launch_stream_hd(const StreamParams& p, const StreamPlan& pl, const 
   using Cfg = StreamCfg<F8 ? 64 : HD>;
   const dim3 grid(pl.units * pl.nsplit);
   const int smem = Cfg::kSmemBytes;
+  if (F8 && pl.rows <= 8)  // fp8 decode: the transposed (keys x rows) MMA form
+    return launch_pdl(gqa_stream_kernel<HD, BF, 1, F8, true>, grid, Cfg::kThreads, smem, st, p, km, vm);
   switch (pl.rg) {
     case 1: return launch_pdl(gqa_stream_kernel<HD, BF, 1, F8>, grid, Cfg::kThreads, smem, st, p, km, vm);
     case 2: return launch_pdl(gqa_stream_kernel<HD, BF, 2, F8>, grid, Cfg::kThreads, smem, st, p, km, vm);

@@ -95,11 +95,17 @@ struct StreamCfg {
 // geometry of a 16-bit HD = 64 row); Q and O keep the 16-bit I/O type. Both MMAs
 // then run in f16: Q is converted once, K and V fragments are converted exactly
 // from e4m3 after ldmatrix, and P is packed as f16 (P <= 1).
-template <int HD, bool BF16, int RG, bool FP8 = false>
+//
+// NT (at most 8 packed rows: decode): the MMAs run transposed, keys as M and the
+// rows as N, so an m16n8k16 carries 16 keys x 8 rows instead of 8 keys x 16 rows
+// of which at most 8 are real: S^T = K Q^T, then O^T += V^T P^T with P^T's
+// fragments from movmatrix. Half the MMAs and half the exp2 work per key.
+template <int HD, bool BF16, int RG, bool FP8 = false, bool NT = false>
 __global__ void __launch_bounds__(288, 1)
     gqa_stream_kernel(const StreamParams p, const __grid_constant__ CUtensorMap kmap,
                       const __grid_constant__ CUtensorMap vmap) {
   static_assert(!FP8 || HD == 128, "fp8 K/V rows are 128 bytes");
+  static_assert(!NT || RG == 1, "the transposed form is the one-row-group kernel");
   using Cfg = StreamCfg<FP8 ? 64 : HD>;  // ring geometry (bytes per key row)
   constexpr bool MMA_BF16 = BF16 && !FP8;  // operand type of both MMAs
   constexpr int NW = Cfg::kWarps;
@@ -110,6 +116,8 @@ __global__ void __launch_bounds__(288, 1)
   constexpr int NKS = HD / 16;          // k16 steps along d
   constexpr int CT = NW * 32;           // compute threads
   static_assert(NKW >= 16, "a warp needs at least one k16 block of keys");
+  static_assert(!NT || NKW == 16, "transposed: one m16 block of keys per warp and stage");
+  constexpr int NACC = NT ? HD / 16 : NDB;  // accumulator fragments
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_base = smem_u32(smem_raw);
@@ -240,25 +248,49 @@ __global__ void __launch_bounds__(288, 1)
   const int gr = lane >> 2;
   const int gc = lane & 3;
 
-  // Packed rows owned by this thread: r0 = rg*16 + gr, r1 = r0 + 8.
+  // Packed rows owned by this thread: r0 = rg*16 + gr, r1 = r0 + 8 (NT: the softmax
+  // rows 2gc, 2gc + 1, and Q row gr for the B fragments).
   int lim_r[2];  // local key limit (exclusive) for each row, clipped to the chunk
   const uint16_t* qrow[2];
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
-    const int r = rg * 16 + gr + 8 * h;
-    const int g = r / p.block_m;
-    const int m = r - g * p.block_m;
-    const int pos = mt * p.block_m + m;
-    const bool valid = (r < p.rows) && (pos < p.seq_q);
+    auto row_pos = [&](int r, int& g) {
+      g = r / p.block_m;
+      return mt * p.block_m + (r - g * p.block_m);
+    };
+    int g;
+    const int rl = NT ? 2 * gc + h : rg * 16 + gr + 8 * h;
+    const int pos_l = row_pos(rl, g);
     int lim = k_end;
-    if (p.causal) lim = min(lim, pos + off - p.kv_offset + 1);
+    if (p.causal) lim = min(lim, pos_l + off - p.kv_offset + 1);
     lim_r[h] = lim;
+    const int rq = NT ? gr : rl;
+    const int pos = row_pos(rq, g);
+    const bool valid = (rq < p.rows) && (pos < p.seq_q) && (!NT || h == 0);
     qrow[h] = valid ? p.q + b * p.q_sb + (int64_t)(kvh * p.group + g) * p.q_sh + (int64_t)pos * p.q_sm : nullptr;
   }
 
   // Q fragments (A operand, 16 rows x HD), loaded once.
   uint32_t qa[NKS][4];
-  if constexpr (FP8) {
+  if constexpr (NT && FP8) {
+    // B fragments of K Q^T: k16 step kk, row gr, d 16kk + 4gc..+3 (the e4m3 order).
+#pragma unroll
+    for (int kk = 0; kk < NKS; ++kk) {
+      const uint2 q0 = qrow[0] ? *reinterpret_cast<const uint2*>(qrow[0] + kk * 16 + gc * 4) : make_uint2(0u, 0u);
+      qa[kk][0] = to_f16x2<BF16>(q0.x);
+      qa[kk][1] = to_f16x2<BF16>(q0.y);
+      qa[kk][2] = qa[kk][3] = 0u;
+    }
+  } else if constexpr (NT) {
+    // B fragments of K Q^T: k16 step kk, row gr, d 16kk + 2gc, +1 and 16kk + 2gc + 8, +9.
+#pragma unroll
+    for (int kk = 0; kk < NKS; ++kk) {
+      const int d0 = kk * 16 + gc * 2;
+      qa[kk][0] = qrow[0] ? *reinterpret_cast<const uint32_t*>(qrow[0] + d0) : 0u;
+      qa[kk][1] = qrow[0] ? *reinterpret_cast<const uint32_t*>(qrow[0] + d0 + 8) : 0u;
+      qa[kk][2] = qa[kk][3] = 0u;
+    }
+  } else if constexpr (FP8) {
     // k16 step kk covers d 16kk..16kk+15 in the order the e4m3 K fragments take
     // (k 2t, 2t+1 -> d 4t, 4t+1; k 2t+8, 2t+9 -> d 4t+2, 4t+3), in f16.
 #pragma unroll
@@ -283,9 +315,9 @@ __global__ void __launch_bounds__(288, 1)
     }
   }
 
-  float acc[NDB][4];
+  float acc[NACC][4];
 #pragma unroll
-  for (int i = 0; i < NDB; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  for (int i = 0; i < NACC; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
   float m_run[2] = {-INFINITY, -INFINITY};
   float l_run[2] = {0.f, 0.f};
   const float scale = p.scale_log2;
@@ -298,123 +330,223 @@ __global__ void __launch_bounds__(288, 1)
     const uint32_t kst = base + slot * Cfg::kStageBytes;
     const uint32_t vst = kst + Cfg::kTileBytes;
     const int key_w = k_begin + t * Cfg::kBN + ks * NKW;  // first key of this warp's block
-    if (key_w < k_end) {  // warp-uniform: blocks past the chunk end were not loaded
-      // ---- S = Q K^T over this warp's NKW keys
-      float s[NNB][4];
-#pragma unroll
-      for (int nb = 0; nb < NNB; ++nb) s[nb][0] = s[nb][1] = s[nb][2] = s[nb][3] = 0.f;
-      if constexpr (FP8) {
-        // A 16-byte chunk of a key row is 16 e4m3 values of d, one k16 step: lane
-        // (g, t) of an 8 x 16-byte ldmatrix gets d 4t..4t+3 of key g, i.e. both B
-        // registers of the step in the order the Q fragments were loaded in.
-#pragma unroll
-        for (int kc = 0; kc < HD / 64; ++kc) {
-#pragma unroll
-          for (int nb = 0; nb < NNB; ++nb) {
-            const int krow = ks * NKW + nb * 8 + (lane & 7);
-            const int chunk = kc * 4 + (lane >> 3);
-            uint32_t r[4];
-            ldsm_x4(kst + sw128_off(krow, chunk), r[0], r[1], r[2], r[3]);
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              mma_16816<false>(s[nb], qa[4 * kc + j], e4m3x2_to_f16x2(r[j]), e4m3x2_to_f16x2(r[j] >> 16));
-          }
-        }
-      } else {
-#pragma unroll
-        for (int kc = 0; kc < HD / 32; ++kc) {
-#pragma unroll
-          for (int nb = 0; nb < NNB; ++nb) {
-            const int krow = ks * NKW + nb * 8 + (lane & 7);
-            const int chunk = kc * 4 + (lane >> 3);
-            const uint32_t addr = kst + (chunk >> 3) * Cfg::kSubBytes + sw128_off(krow, chunk & 7);
-            uint32_t b0, b1, b2, b3;
-            ldsm_x4(addr, b0, b1, b2, b3);
-            mma_16816<BF16>(s[nb], qa[2 * kc], b0, b1);
-            mma_16816<BF16>(s[nb], qa[2 * kc + 1], b2, b3);
-          }
-        }
-      }
-
-      // ---- online softmax (log2 domain)
-      float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-      for (int nb = 0; nb < NNB; ++nb) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int h = e >> 1;
-          const int key = key_w + nb * 8 + gc * 2 + (e & 1);
-          const float x = (key < lim_r[h]) ? s[nb][e] * scale : -INFINITY;
-          s[nb][e] = x;
-          mx[h] = fmaxf(mx[h], x);
-        }
-      }
-      float alpha[2], mu[2];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
-        mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
-        const float m_new = fmaxf(m_run[h], mx[h]);
-        mu[h] = (m_new == -INFINITY) ? 0.f : m_new;  // keeps fully-masked rows at p = 0, not NaN
-        alpha[h] = fast_exp2(m_run[h] - mu[h]);
-        m_run[h] = m_new;
-      }
-      float lsum[2] = {0.f, 0.f};
-#pragma unroll
-      for (int nb = 0; nb < NNB; ++nb) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float pv = fast_exp2(s[nb][e] - mu[e >> 1]);
-          s[nb][e] = pv;
-          lsum[e >> 1] += pv;
-        }
-      }
-#pragma unroll
-      for (int h = 0; h < 2; ++h) l_run[h] = l_run[h] * alpha[h] + lsum[h];
-#pragma unroll
-      for (int i = 0; i < NDB; ++i) {
-        acc[i][0] *= alpha[0];
-        acc[i][1] *= alpha[0];
-        acc[i][2] *= alpha[1];
-        acc[i][3] *= alpha[1];
-      }
-
-      // ---- O += P V
-#pragma unroll
-      for (int kk = 0; kk < NKW / 16; ++kk) {
-        uint32_t pa[4];
-        pa[0] = pack2<MMA_BF16>(s[2 * kk][0], s[2 * kk][1]);
-        pa[1] = pack2<MMA_BF16>(s[2 * kk][2], s[2 * kk][3]);
-        pa[2] = pack2<MMA_BF16>(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-        pa[3] = pack2<MMA_BF16>(s[2 * kk + 1][2], s[2 * kk + 1][3]);
-        const int vrow = ks * NKW + kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+    if constexpr (NT) {
+      if (key_w < k_end) {
+        // ---- S^T = K Q^T: 16 keys (M) x 8 rows (N). Two partial sums (even and odd
+        // k16 steps) keep two MMA chains in flight. A 16-byte chunk of a key row is
+        // one k16 step; ldmatrix gives lane (g, t) d 4t..4t+3 of keys g and g + 8.
+        float st[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        const int krow = ks * NKW + (lane & 7) + ((lane >> 3) & 1) * 8;
         if constexpr (FP8) {
-          // Transposed 8 x 16-byte loads of keys 0-7 and 8-15 of 16-d chunks c, c+1:
-          // lane (g, t) gets keys 2t, 2t+1 x d 2g, 2g+1 of each. Bytes (0, 2) are the
-          // B pair of column d = 2g, bytes (1, 3) that of d = 2g + 1, so chunk c
-          // feeds accumulator blocks 2c (even d) and 2c + 1 (odd d).
 #pragma unroll
           for (int c = 0; c < HD / 16; c += 2) {
-            const int chunk = c + (lane >> 4);
             uint32_t r[4];
-            ldsm_x4_t(vst + sw128_off(vrow, chunk), r[0], r[1], r[2], r[3]);
+            ldsm_x4(kst + sw128_off(krow, c + (lane >> 4)), r[0], r[1], r[2], r[3]);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {  // chunk c + h: keys 0-7 in r[2h], keys 8-15 in r[2h + 1]
+              const uint32_t a[4] = {e4m3x2_to_f16x2(r[2 * h]), e4m3x2_to_f16x2(r[2 * h + 1]),
+                                     e4m3x2_to_f16x2(r[2 * h] >> 16), e4m3x2_to_f16x2(r[2 * h + 1] >> 16)};
+              mma_16816<false>(st[h], a, qa[c + h][0], qa[c + h][1]);
+            }
+          }
+        } else {
+          // k16 step kk = 16-byte chunks 2kk, 2kk + 1 of keys 0-7 and 8-15: the four
+          // matrices of one ldmatrix are the A fragment as they land.
+#pragma unroll
+          for (int kk = 0; kk < NKS; ++kk) {
+            const int chunk = 2 * kk + (lane >> 4);
+            uint32_t a[4];
+            ldsm_x4(kst + (chunk >> 3) * Cfg::kSubBytes + sw128_off(krow, chunk & 7), a[0], a[1], a[2], a[3]);
+            mma_16816<MMA_BF16>(st[kk & 1], a, qa[kk][0], qa[kk][1]);
+          }
+        }
+        // s[e]: key gr + 8 (e >> 1), row 2gc + (e & 1)
+        float s[4], mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int key = key_w + gr + 8 * (e >> 1);
+          const float x = (key < lim_r[e & 1]) ? (st[0][e] + st[1][e]) * scale : -INFINITY;
+          s[e] = x;
+          mx[e & 1] = fmaxf(mx[e & 1], x);
+        }
+        float alpha[2], mu[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {  // rows are spread over the lanes of one gc
+          mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 4));
+          mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 8));
+          mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 16));
+          const float m_new = fmaxf(m_run[h], mx[h]);
+          mu[h] = (m_new == -INFINITY) ? 0.f : m_new;  // keeps fully-masked rows at p = 0, not NaN
+          alpha[h] = fast_exp2(m_run[h] - mu[h]);
+          m_run[h] = m_new;
+        }
+        float lsum[2] = {0.f, 0.f};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          s[e] = fast_exp2(s[e] - mu[e & 1]);
+          lsum[e & 1] += s[e];
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) l_run[h] = l_run[h] * alpha[h] + lsum[h];
+#pragma unroll
+        for (int c = 0; c < NACC; ++c) {  // acc[c]: rows 2gc, 2gc + 1, 2gc, 2gc + 1
+          acc[c][0] *= alpha[0];
+          acc[c][1] *= alpha[1];
+          acc[c][2] *= alpha[0];
+          acc[c][3] *= alpha[1];
+        }
+        // ---- O^T += V^T P^T. P^T's B fragments: the 8 x 8 (key, row) blocks of P
+        // transposed in registers. V^T's A fragments: transposed 8 x 16-byte loads of
+        // keys 0-7 and 8-15; bytes (0, 2) are keys 2t, 2t + 1 at d = 2g (A row g),
+        // bytes (1, 3) the same keys at d = 2g + 1 (A row g + 8).
+        const uint32_t pb0 = movmatrix_t(pack2<MMA_BF16>(s[0], s[1]));  // keys 0-7
+        const uint32_t pb1 = movmatrix_t(pack2<MMA_BF16>(s[2], s[3]));  // keys 8-15
+        if constexpr (FP8) {
+#pragma unroll
+          for (int c = 0; c < HD / 16; c += 2) {
+            uint32_t r[4];
+            ldsm_x4_t(vst + sw128_off(krow, c + (lane >> 4)), r[0], r[1], r[2], r[3]);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-              const uint32_t lo = prmt(r[2 * h], 0u, 0x3120u);      // keys 0-7:  even pair | odd pair
+              const uint32_t lo = prmt(r[2 * h], 0u, 0x3120u);      // keys 0-7:  d even pair | d odd pair
               const uint32_t hi = prmt(r[2 * h + 1], 0u, 0x3120u);  // keys 8-15
-              mma_16816<false>(acc[2 * (c + h)], pa, e4m3x2_to_f16x2(lo), e4m3x2_to_f16x2(hi));
-              mma_16816<false>(acc[2 * (c + h) + 1], pa, e4m3x2_to_f16x2(lo >> 16), e4m3x2_to_f16x2(hi >> 16));
+              const uint32_t a[4] = {e4m3x2_to_f16x2(lo), e4m3x2_to_f16x2(lo >> 16), e4m3x2_to_f16x2(hi),
+                                     e4m3x2_to_f16x2(hi >> 16)};
+              mma_16816<false>(acc[c + h], a, pb0, pb1);
+            }
+          }
+        } else {
+          // d tile c (A rows = d 16c..16c+15): transposed loads of (keys 0-7, d lo),
+          // (keys 0-7, d hi), (keys 8-15, d lo), (keys 8-15, d hi) are a0..a3.
+          const int vrow = ks * NKW + (lane & 7) + (lane >> 4) * 8;
+#pragma unroll
+          for (int c = 0; c < NACC; ++c) {
+            const int chunk = 2 * c + ((lane >> 3) & 1);
+            uint32_t a[4];
+            ldsm_x4_t(vst + (chunk >> 3) * Cfg::kSubBytes + sw128_off(vrow, chunk & 7), a[0], a[1], a[2], a[3]);
+            mma_16816<MMA_BF16>(acc[c], a, pb0, pb1);
+          }
+        }
+      }
+    } else {
+      if (key_w < k_end) {  // warp-uniform: blocks past the chunk end were not loaded
+        // ---- S = Q K^T over this warp's NKW keys
+        float s[NNB][4];
+#pragma unroll
+        for (int nb = 0; nb < NNB; ++nb) s[nb][0] = s[nb][1] = s[nb][2] = s[nb][3] = 0.f;
+        if constexpr (FP8) {
+          // A 16-byte chunk of a key row is 16 e4m3 values of d, one k16 step: lane
+          // (g, t) of an 8 x 16-byte ldmatrix gets d 4t..4t+3 of key g, i.e. both B
+          // registers of the step in the order the Q fragments were loaded in.
+#pragma unroll
+          for (int kc = 0; kc < HD / 64; ++kc) {
+#pragma unroll
+            for (int nb = 0; nb < NNB; ++nb) {
+              const int krow = ks * NKW + nb * 8 + (lane & 7);
+              const int chunk = kc * 4 + (lane >> 3);
+              uint32_t r[4];
+              ldsm_x4(kst + sw128_off(krow, chunk), r[0], r[1], r[2], r[3]);
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                mma_16816<false>(s[nb], qa[4 * kc + j], e4m3x2_to_f16x2(r[j]), e4m3x2_to_f16x2(r[j] >> 16));
             }
           }
         } else {
 #pragma unroll
-          for (int dc = 0; dc < NDB; dc += 2) {
-            const int chunk = dc + (lane >> 4);
-            const uint32_t addr = vst + (chunk >> 3) * Cfg::kSubBytes + sw128_off(vrow, chunk & 7);
-            uint32_t b0, b1, b2, b3;
-            ldsm_x4_t(addr, b0, b1, b2, b3);
-            mma_16816<BF16>(acc[dc], pa, b0, b1);
-            mma_16816<BF16>(acc[dc + 1], pa, b2, b3);
+          for (int kc = 0; kc < HD / 32; ++kc) {
+#pragma unroll
+            for (int nb = 0; nb < NNB; ++nb) {
+              const int krow = ks * NKW + nb * 8 + (lane & 7);
+              const int chunk = kc * 4 + (lane >> 3);
+              const uint32_t addr = kst + (chunk >> 3) * Cfg::kSubBytes + sw128_off(krow, chunk & 7);
+              uint32_t b0, b1, b2, b3;
+              ldsm_x4(addr, b0, b1, b2, b3);
+              mma_16816<BF16>(s[nb], qa[2 * kc], b0, b1);
+              mma_16816<BF16>(s[nb], qa[2 * kc + 1], b2, b3);
+            }
+          }
+        }
+
+        // ---- online softmax (log2 domain)
+        float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int nb = 0; nb < NNB; ++nb) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int h = e >> 1;
+            const int key = key_w + nb * 8 + gc * 2 + (e & 1);
+            const float x = (key < lim_r[h]) ? s[nb][e] * scale : -INFINITY;
+            s[nb][e] = x;
+            mx[h] = fmaxf(mx[h], x);
+          }
+        }
+        float alpha[2], mu[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+          mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+          const float m_new = fmaxf(m_run[h], mx[h]);
+          mu[h] = (m_new == -INFINITY) ? 0.f : m_new;  // keeps fully-masked rows at p = 0, not NaN
+          alpha[h] = fast_exp2(m_run[h] - mu[h]);
+          m_run[h] = m_new;
+        }
+        float lsum[2] = {0.f, 0.f};
+#pragma unroll
+        for (int nb = 0; nb < NNB; ++nb) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float pv = fast_exp2(s[nb][e] - mu[e >> 1]);
+            s[nb][e] = pv;
+            lsum[e >> 1] += pv;
+          }
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) l_run[h] = l_run[h] * alpha[h] + lsum[h];
+#pragma unroll
+        for (int i = 0; i < NDB; ++i) {
+          acc[i][0] *= alpha[0];
+          acc[i][1] *= alpha[0];
+          acc[i][2] *= alpha[1];
+          acc[i][3] *= alpha[1];
+        }
+
+        // ---- O += P V
+#pragma unroll
+        for (int kk = 0; kk < NKW / 16; ++kk) {
+          uint32_t pa[4];
+          pa[0] = pack2<MMA_BF16>(s[2 * kk][0], s[2 * kk][1]);
+          pa[1] = pack2<MMA_BF16>(s[2 * kk][2], s[2 * kk][3]);
+          pa[2] = pack2<MMA_BF16>(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+          pa[3] = pack2<MMA_BF16>(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+          const int vrow = ks * NKW + kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+          if constexpr (FP8) {
+            // Transposed 8 x 16-byte loads of keys 0-7 and 8-15 of 16-d chunks c, c+1:
+            // lane (g, t) gets keys 2t, 2t+1 x d 2g, 2g+1 of each. Bytes (0, 2) are the
+            // B pair of column d = 2g, bytes (1, 3) that of d = 2g + 1, so chunk c
+            // feeds accumulator blocks 2c (even d) and 2c + 1 (odd d).
+#pragma unroll
+            for (int c = 0; c < HD / 16; c += 2) {
+              const int chunk = c + (lane >> 4);
+              uint32_t r[4];
+              ldsm_x4_t(vst + sw128_off(vrow, chunk), r[0], r[1], r[2], r[3]);
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const uint32_t lo = prmt(r[2 * h], 0u, 0x3120u);      // keys 0-7:  even pair | odd pair
+                const uint32_t hi = prmt(r[2 * h + 1], 0u, 0x3120u);  // keys 8-15
+                mma_16816<false>(acc[2 * (c + h)], pa, e4m3x2_to_f16x2(lo), e4m3x2_to_f16x2(hi));
+                mma_16816<false>(acc[2 * (c + h) + 1], pa, e4m3x2_to_f16x2(lo >> 16), e4m3x2_to_f16x2(hi >> 16));
+              }
+            }
+          } else {
+#pragma unroll
+            for (int dc = 0; dc < NDB; dc += 2) {
+              const int chunk = dc + (lane >> 4);
+              const uint32_t addr = vst + (chunk >> 3) * Cfg::kSubBytes + sw128_off(vrow, chunk & 7);
+              uint32_t b0, b1, b2, b3;
+              ldsm_x4_t(addr, b0, b1, b2, b3);
+              mma_16816<BF16>(acc[dc], pa, b0, b1);
+              mma_16816<BF16>(acc[dc + 1], pa, b2, b3);
+            }
           }
         }
       }
@@ -423,11 +555,18 @@ __global__ void __launch_bounds__(288, 1)
     if (lane == 0) mbar_arrive(bar_empty + 8 * slot);
   }
 
-  // Row sums are per-thread partials over the quad's columns.
+  // Row sums are per-thread partials over the quad's columns (NT: over the lanes
+  // of one gc, which hold the keys).
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
-    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 1);
-    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 2);
+    if constexpr (NT) {
+      l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 4);
+      l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 8);
+      l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 16);
+    } else {
+      l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 1);
+      l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 2);
+    }
   }
 
   // ---- merge the KS warps of each row group through shared memory
@@ -443,7 +582,26 @@ __global__ void __launch_bounds__(288, 1)
   {
     float* aw = abuf + warp * 16 * AS;
     const bool upper = rg * 16 + 8 < p.rows;  // warp-uniform
-    if constexpr (FP8) {
+    if constexpr (NT && FP8) {
+      // acc[c]: d 16c + 2gr (+1 in [2], [3]) of rows 2gc ([0], [2]) and 2gc + 1.
+      const float vs = p.v_scale;
+#pragma unroll
+      for (int c = 0; c < NACC; ++c) {
+        const int d = c * 16 + gr * 2;
+        *reinterpret_cast<float2*>(aw + (2 * gc) * AS + d) = make_float2(acc[c][0] * vs, acc[c][2] * vs);
+        *reinterpret_cast<float2*>(aw + (2 * gc + 1) * AS + d) = make_float2(acc[c][1] * vs, acc[c][3] * vs);
+      }
+    } else if constexpr (NT) {
+      // acc[c]: d 16c + gr ([0], [1]) and 16c + gr + 8 ([2], [3]) of rows 2gc, 2gc + 1.
+#pragma unroll
+      for (int c = 0; c < NACC; ++c) {
+        const int d = c * 16 + gr;
+        aw[(2 * gc) * AS + d] = acc[c][0];
+        aw[(2 * gc + 1) * AS + d] = acc[c][1];
+        aw[(2 * gc) * AS + d + 8] = acc[c][2];
+        aw[(2 * gc + 1) * AS + d + 8] = acc[c][3];
+      }
+    } else if constexpr (FP8) {
       // Blocks 2c, 2c + 1 hold d = 16c + 4t + {0, 2} and {1, 3}: four consecutive d.
       const float vs = p.v_scale;
 #pragma unroll
@@ -464,7 +622,15 @@ __global__ void __launch_bounds__(288, 1)
         if (upper) *reinterpret_cast<float2*>(aw + (gr + 8) * AS + d) = make_float2(acc[i][2], acc[i][3]);
       }
     }
-    if (gc == 0) {
+    if constexpr (NT) {
+      if (gr < 2) {  // rows 2gc, 2gc + 1 (gr 0); rows 8..15 do not exist (gr 1)
+        const int r = 8 * gr + 2 * gc;
+        mbuf[warp * 16 + r] = gr ? -INFINITY : m_run[0];
+        mbuf[warp * 16 + r + 1] = gr ? -INFINITY : m_run[1];
+        lbuf[warp * 16 + r] = gr ? 0.f : l_run[0];
+        lbuf[warp * 16 + r + 1] = gr ? 0.f : l_run[1];
+      }
+    } else if (gc == 0) {
       mbuf[warp * 16 + gr] = m_run[0];
       mbuf[warp * 16 + gr + 8] = m_run[1];
       lbuf[warp * 16 + gr] = l_run[0];
