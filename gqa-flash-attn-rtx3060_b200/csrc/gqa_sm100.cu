@@ -333,7 +333,7 @@ cudaError_t launch_stream_hd(const StreamParams& p, const StreamPlan& pl, const 
   using Cfg = StreamCfg<F8 ? 64 : HD>;
   const dim3 grid(pl.units * pl.nsplit);
   const int smem = Cfg::kSmemBytes;
-  if (F8 && pl.rows <= 8)  // fp8 decode: the transposed (keys x rows) MMA form
+  if (pl.rows <= 8)  // decode: the transposed (keys x rows) MMA form
     return launch_pdl(gqa_stream_kernel<HD, BF, 1, F8, true>, grid, Cfg::kThreads, smem, st, p, km, vm);
   switch (pl.rg) {
     case 1: return launch_pdl(gqa_stream_kernel<HD, BF, 1, F8>, grid, Cfg::kThreads, smem, st, p, km, vm);
