@@ -81,13 +81,12 @@ def paged_decode(query, key_cache, value_cache, block_tables, seq_lens, max_seq_
 
 
 def _check_cache(query, key_cache, value_cache, block_tables, seq_lens, num_seqs, num_heads, head_dim):
+    """Shapes, dtypes and layout first, the device last, so every check runs on CPU tensors."""
     num_blocks, block_size, num_kv_heads, hd = key_cache.shape
     if hd != head_dim or value_cache.shape != key_cache.shape:
         raise ValueError("key_cache and value_cache must be (num_blocks, block_size, num_kv_heads, head_dim)")
     if num_heads % num_kv_heads:
         raise ValueError("num_heads must be divisible by num_kv_heads")
-    if not (query.is_cuda and key_cache.is_cuda and value_cache.is_cuda):
-        raise ValueError("tensors must be on a CUDA device")
     if key_cache.dtype != value_cache.dtype or key_cache.dtype not in (query.dtype, torch.float8_e4m3fn):
         raise TypeError("the caches must share query's dtype, or both be float8_e4m3fn")
     if not (key_cache.is_contiguous() and value_cache.is_contiguous()):
@@ -96,6 +95,8 @@ def _check_cache(query, key_cache, value_cache, block_tables, seq_lens, num_seqs
         raise TypeError("block_tables and seq_lens must be int32")
     if block_tables.dim() != 2 or block_tables.shape[0] != num_seqs or seq_lens.shape != (num_seqs,):
         raise ValueError("block_tables must be (num_seqs, max_blocks) and seq_lens (num_seqs,)")
+    if not all(t.is_cuda for t in (query, key_cache, value_cache, block_tables, seq_lens)):
+        raise ValueError("tensors must be on a CUDA device")
     return num_blocks, block_size, num_kv_heads
 
 

@@ -1,0 +1,69 @@
+"""Argument checks of the paged-attention API (gqa_kernels.paged) on CPU tensors: every
+malformed call raises before anything is launched, so these run without a GPU."""
+import pytest
+import torch
+
+from gqa_kernels.paged import paged_decode, paged_prefill
+
+
+def _cache(num_blocks=4, block_size=64, hkv=2, D=128, dtype=torch.bfloat16):
+    return torch.zeros(num_blocks, block_size, hkv, D, dtype=dtype), torch.zeros(num_blocks, block_size, hkv, D,
+                                                                                  dtype=dtype)
+
+
+def _meta(n=2, max_blocks=2):
+    return torch.zeros(n, max_blocks, dtype=torch.int32), torch.full((n,), 10, dtype=torch.int32)
+
+
+def test_cache_shape_and_heads():
+    kc, vc = _cache()
+    bt, sl = _meta()
+    q = torch.zeros(2, 8, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="num_blocks, block_size"):
+        paged_decode(q, kc, vc[:, :, :, :64], bt, sl)
+    with pytest.raises(ValueError, match="num_blocks, block_size"):
+        paged_decode(torch.zeros(2, 8, 64, dtype=torch.bfloat16), kc, vc, bt, sl)
+    with pytest.raises(ValueError, match="divisible"):
+        paged_decode(torch.zeros(2, 7, 128, dtype=torch.bfloat16), kc, vc, bt, sl)
+
+
+def test_tensors_must_be_on_the_gpu():
+    kc, vc = _cache()
+    bt, sl = _meta()
+    with pytest.raises(ValueError, match="CUDA"):
+        paged_decode(torch.zeros(2, 8, 128, dtype=torch.bfloat16), kc, vc, bt, sl)
+    with pytest.raises(ValueError, match="CUDA"):
+        paged_prefill(torch.zeros(2, 8, 16, 128, dtype=torch.bfloat16), kc, vc, bt, sl)
+
+
+def test_dtypes():
+    kc, vc = _cache(dtype=torch.float16)
+    bt, sl = _meta()
+    q = torch.zeros(2, 8, 4, 128, dtype=torch.bfloat16)
+    with pytest.raises(TypeError, match="dtype"):
+        paged_prefill(q, kc, vc, bt, sl)  # fp16 caches under bf16 queries
+    k8, v8 = _cache(dtype=torch.float8_e4m3fn)
+    with pytest.raises(TypeError, match="dtype"):
+        paged_prefill(q, k8, vc, bt, sl)  # mixed cache dtypes
+
+
+def test_block_table_and_lengths():
+    kc, vc = _cache()
+    q = torch.zeros(2, 8, 128, dtype=torch.bfloat16)
+    bt, sl = _meta()
+    with pytest.raises(TypeError, match="int32"):
+        paged_decode(q, kc, vc, bt.long(), sl)
+    with pytest.raises(TypeError, match="int32"):
+        paged_decode(q, kc, vc, bt, sl.long())
+    with pytest.raises(ValueError, match="num_seqs"):
+        paged_decode(q, kc, vc, bt[:1], sl)
+    with pytest.raises(ValueError, match="num_seqs"):
+        paged_decode(q, kc, vc, bt, sl[:1])
+
+
+def test_caches_must_be_contiguous():
+    kc, vc = _cache()
+    bt, sl = _meta()
+    q = torch.zeros(2, 8, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="contiguous"):
+        paged_decode(q, kc.transpose(0, 1).contiguous().transpose(0, 1), vc, bt, sl)
