@@ -90,6 +90,17 @@ def check(code, what):
         raise RuntimeError(f"{what} failed: {strerror(code)} (status {code})")
 
 
+def check_one_device(*tensors):
+    """Every tensor a launch reads or writes must be CUDA memory of one device: the
+    kernels take raw pointers and run on the first tensor's device."""
+    dev = tensors[0].device
+    for t in tensors:
+        if not t.is_cuda:
+            raise ValueError("tensors must be on a CUDA device")
+        if t.device != dev:
+            raise ValueError("tensors must be on one device")
+
+
 def strides(t, n=4):
     """Element strides of `t` as a ctypes int64 array."""
     return (ctypes.c_int64 * n)(*t.stride())

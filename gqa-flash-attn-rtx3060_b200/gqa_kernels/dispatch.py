@@ -65,6 +65,8 @@ def _gqa_flash_attn(q, k, v, causal=True):
     group_size = num_heads // num_kv_heads
     assert head_dim in (64, 128), f"unsupported head_dim {head_dim}"
     assert q.is_cuda and k.is_cuda and v.is_cuda
+    if not (q.device == k.device == v.device):  # one device's memory per launch
+        raise ValueError("q, k and v must be on one device")
     if tuple(v.shape) != tuple(k.shape):
         raise ValueError("k and v must have the same shape")
     if not (q.dtype == k.dtype == v.dtype):

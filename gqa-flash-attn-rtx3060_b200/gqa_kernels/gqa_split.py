@@ -23,6 +23,7 @@ LOG2E = 1.4426950408889634
 
 def split_kv_forward(q, k, v, causal, splits):
     """Split-KV forward (one fused launch). Call from dispatch when seq_q is small."""
+    _lib.check_one_device(q, k, v)
     batch, num_heads, seq_q, head_dim = q.shape
     _, num_kv_heads, seq_kv, _ = k.shape
     scale_log2 = (head_dim ** -0.5) * LOG2E
@@ -116,6 +117,7 @@ gqa_split_reduce_kernel = _SplitReduceLauncher()
 def split_kv_two_pass(q, k, v, causal, splits):
     """The reference's two-launch split-KV forward, kept for API parity and tests:
     partials (m_p, l_p, acc_p) through gqa_split_first, combine through gqa_split_reduce."""
+    _lib.check_one_device(q, k, v)
     batch, num_heads, seq_q, head_dim = q.shape
     _, num_kv_heads, seq_kv, _ = k.shape
     group_size = num_heads // num_kv_heads

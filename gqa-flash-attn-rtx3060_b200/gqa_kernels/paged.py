@@ -95,8 +95,7 @@ def _check_cache(query, key_cache, value_cache, block_tables, seq_lens, num_seqs
         raise TypeError("block_tables and seq_lens must be int32")
     if block_tables.dim() != 2 or block_tables.shape[0] != num_seqs or seq_lens.shape != (num_seqs,):
         raise ValueError("block_tables must be (num_seqs, max_blocks) and seq_lens (num_seqs,)")
-    if not all(t.is_cuda for t in (query, key_cache, value_cache, block_tables, seq_lens)):
-        raise ValueError("tensors must be on a CUDA device")
+    _lib.check_one_device(query, key_cache, value_cache, block_tables, seq_lens)
     return num_blocks, block_size, num_kv_heads
 
 

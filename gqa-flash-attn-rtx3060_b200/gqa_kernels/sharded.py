@@ -78,6 +78,7 @@ def partial_forward(q, k_shard, v_shard, causal, kv_offset, seq_kv_total, out=No
     m, l: batch*num_heads*seq_q values each; acc: rows x head_dim (packed_layout
     gives the offsets). `out` may be a preallocated buffer of packed_size() elements.
     """
+    _lib.check_one_device(q, k_shard, v_shard, *(() if out is None else (out,)))
     batch, num_heads, seq_q, head_dim = q.shape
     _, num_kv_heads, n_local, _ = k_shard.shape
     rows, acc_off, total = packed_layout(q.shape)

@@ -67,3 +67,14 @@ def test_caches_must_be_contiguous():
     q = torch.zeros(2, 8, 128, dtype=torch.bfloat16)
     with pytest.raises(ValueError, match="contiguous"):
         paged_decode(q, kc.transpose(0, 1).contiguous().transpose(0, 1), vc, bt, sl)
+
+
+def test_split_and_partial_entry_points_refuse_host_tensors():
+    from gqa_kernels import sharded
+    from gqa_kernels.gqa_split import split_kv_forward, split_kv_two_pass
+    q = torch.zeros(1, 8, 1, 128, dtype=torch.bfloat16)
+    k = torch.zeros(1, 2, 2048, 128, dtype=torch.bfloat16)
+    for fn in (lambda: split_kv_forward(q, k, k, True, 4), lambda: split_kv_two_pass(q, k, k, True, 4),
+               lambda: sharded.partial_forward(q, k, k, True, 0, 2048)):
+        with pytest.raises(ValueError, match="CUDA"):
+            fn()

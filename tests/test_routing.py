@@ -14,6 +14,7 @@ GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "routi
 class _Fake:
     is_cuda = True
     dtype = "bf16"
+    device = "cuda:0"
 
     def __init__(self, shape):
         self.shape = tuple(shape)
