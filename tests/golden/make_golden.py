@@ -1,6 +1,6 @@
 """Generates the golden fixtures in tests/golden/ from the reference project itself.
 
-    TRITON_INTERPRET=1 python tests/golden/make_golden.py [/path/to/reference]
+    TRITON_INTERPRET=1 python tests/golden/make_golden.py /path/to/reference
 
 Run once, where the reference checkout exists (it is not needed afterwards):
   * oracle_bf16.npz -- the reference's oracle (tests/reference.py:gqa_reference)
@@ -30,7 +30,9 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("GQA_REFERENCE_DIR", "")
+if not REF or not os.path.isdir(REF):
+    sys.exit("usage: make_golden.py /path/to/reference (or set GQA_REFERENCE_DIR)")
 sys.path.insert(0, REF)
 
 from tests.reference import gqa_reference  # noqa: E402  (reference oracle)
