@@ -14,6 +14,9 @@ It restates, in numpy, the reference project's algorithms for this path:
   route                  gqa_kernels/dispatch.py:37-45     single-pass vs split-KV choice
   partial_attention      (new) partials of one key shard, the multi-GPU split of the key axis
   lse_combine            gqa_kernels/gqa_split.py:137-144 applied across shards
+  paged_reference        (new) the reference attention over a vLLM-layout paged cache:
+                         each sequence's keys gathered through its block table, its
+                         queries bottom-right aligned to its own length
 
 Parity pins: tests/test_oracle_golden.py checks these functions against
 tests/golden/*.npz, produced by tests/golden/make_golden.py from the
@@ -302,3 +305,32 @@ def lse_combine(ms, ls, accs):
     w = np.exp2(ms - Mu[None])
     with np.errstate(invalid="ignore", divide="ignore"):
         return (w[..., None] * accs).sum(axis=0) / (w * ls).sum(axis=0)[..., None]
+
+
+def paged_reference(q, k_cache, v_cache, block_tables, seq_lens, causal=True, k_scale=1.0, v_scale=1.0):
+    """Attention of each sequence's chunk over a paged cache, by gathering.
+
+    q: (num_seqs, Hq, Sq, D); k_cache, v_cache: (num_blocks, block_size, Hkv, D);
+    block_tables: (num_seqs, max_blocks) int; seq_lens: (num_seqs,) int. Key k of
+    sequence b is k_cache[block_tables[b, k // block_size], k % block_size] * k_scale
+    (values likewise with v_scale); its Sq queries are its last Sq positions
+    (tests/reference.py:6-34's bottom-right rule per sequence). Returns float32
+    (num_seqs, Hq, Sq, D); rows that see no key are NaN.
+    """
+    q = np.asarray(q, dtype=np.float32)
+    kc = np.asarray(k_cache, dtype=np.float32)
+    vc = np.asarray(v_cache, dtype=np.float32)
+    n, Hq, Sq, D = q.shape
+    bs = kc.shape[1]
+    out = np.empty((n, Hq, Sq, D), dtype=np.float32)
+    for b in range(n):
+        s = int(seq_lens[b])
+        idx = np.arange(s)
+        blocks = np.asarray(block_tables[b])[idx // bs]
+        k = (kc[blocks, idx % bs] * np.float32(k_scale)).transpose(1, 0, 2)[None]  # (1, Hkv, s, D)
+        v = (vc[blocks, idx % bs] * np.float32(v_scale)).transpose(1, 0, 2)[None]
+        if s == 0:
+            out[b] = np.nan
+        else:
+            out[b] = gqa_reference(q[b:b + 1], k, v, causal=causal)[0]
+    return out

@@ -84,3 +84,15 @@ def test_fp8_unsupported_shapes_raise():
     kc64, vc64, bt64, sl64 = _cache8([300], 8, 64, seed=2, D=64)
     with pytest.raises(RuntimeError, match="unsupported"):
         paged_decode(torch.randn(1, 32, 64, device="cuda").bfloat16(), kc64, vc64, bt64, sl64)
+
+
+def test_fp8_against_the_numpy_oracle():
+    from oracle import gqa_oracle as O
+    seq_lens = [1, 300, 2000]
+    kc, vc, bt, sl = _cache8(seq_lens, 2, 64, seed=77)
+    q = torch.randn(len(seq_lens), 8, 128, device="cuda").bfloat16()
+    out = paged_decode(q, kc, vc, bt, sl, k_scale=0.5, v_scale=1.25)
+    torch.cuda.synchronize()
+    ref = O.paged_reference(to_np(q[:, :, None]), kc.float().cpu().numpy(), vc.float().cpu().numpy(),
+                            bt.cpu().numpy(), seq_lens, causal=True, k_scale=0.5, v_scale=1.25)
+    compare(to_np(out[:, :, None]), ref, BASELINE_TOL)

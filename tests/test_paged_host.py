@@ -78,3 +78,34 @@ def test_split_and_partial_entry_points_refuse_host_tensors():
                lambda: sharded.partial_forward(q, k, k, True, 0, 2048)):
         with pytest.raises(ValueError, match="CUDA"):
             fn()
+
+
+def test_paged_oracle_equals_the_dense_oracle_on_gathered_keys():
+    """oracle.paged_reference against gqa_reference on the same keys laid out densely:
+    shuffled blocks, lengths below, at and above the chunk, an empty sequence, scales."""
+    import numpy as np
+    from oracle import gqa_oracle as O
+    rng = np.random.default_rng(0)
+    bs, Hkv, Hq, D, Sq = 16, 2, 8, 32, 5
+    seq_lens = [3, 5, 40, 0]
+    n_blocks = sum(-(-s // bs) for s in seq_lens) + 2
+    kc = rng.standard_normal((n_blocks, bs, Hkv, D)).astype(np.float32)
+    vc = rng.standard_normal((n_blocks, bs, Hkv, D)).astype(np.float32)
+    perm = rng.permutation(n_blocks)
+    bt = np.zeros((len(seq_lens), 3), dtype=np.int32)
+    c = 0
+    for i, s in enumerate(seq_lens):
+        for j in range(-(-s // bs)):
+            bt[i, j] = perm[c]
+            c += 1
+    q = rng.standard_normal((len(seq_lens), Hq, Sq, D)).astype(np.float32)
+    out = O.paged_reference(q, kc, vc, bt, seq_lens, causal=True, k_scale=0.5, v_scale=2.0)
+    for i, s in enumerate(seq_lens):
+        if s == 0:
+            assert np.isnan(out[i]).all()
+            continue
+        k = np.concatenate([kc[bt[i, j]] for j in range(-(-s // bs))])[:s].transpose(1, 0, 2)[None] * 0.5
+        v = np.concatenate([vc[bt[i, j]] for j in range(-(-s // bs))])[:s].transpose(1, 0, 2)[None] * 2.0
+        ref = O.gqa_reference(q[i:i + 1], k, v, causal=True)[0]
+        np.testing.assert_allclose(out[i], ref, rtol=1e-6, atol=1e-6, equal_nan=True)
+    assert np.isnan(out[0, :, :2]).all() and not np.isnan(out[0, :, 2:]).any()  # 3 keys, 5 queries

@@ -143,3 +143,17 @@ def test_paged_prefill_in_a_cuda_graph():
         g.replay()
     torch.cuda.synchronize()
     assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+
+
+@pytest.mark.parametrize("chunk", [1, 8, 100])
+def test_paged_against_the_numpy_oracle(chunk):
+    """oracle.paged_reference (the reference attention over the gathered blocks) on a
+    small case: decode, a streaming-kernel chunk and a tcgen05 chunk."""
+    from oracle import gqa_oracle as O
+    seq_lens = [chunk, 130, 700]
+    kc, vc, bt, sl = _cache(seq_lens, 2, 128, 64, seed=chunk, dtype=torch.bfloat16)
+    q = torch.randn(len(seq_lens), 8, chunk, 128, device="cuda").bfloat16()
+    out = paged_prefill(q, kc, vc, bt, sl)
+    torch.cuda.synchronize()
+    ref = O.paged_reference(to_np(q), to_np(kc), to_np(vc), bt.cpu().numpy(), seq_lens, causal=True)
+    compare(to_np(out), ref, BASELINE_TOL)
