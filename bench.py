@@ -265,6 +265,86 @@ def make_flush(device):
     return flush
 
 
+# ----------------------------------------------------------------------------- in-run parity
+CHECK_TOL = (2e-2, 2e-3)  # BASELINE contract: max-abs 2e-2, mean-abs 2e-3 against fp32
+
+
+def check_rows_sel(q_shape, n, seed=1234):
+    """n seeded (batch, head, position) rows of an output of shape (B, Hq, Sq, D)."""
+    B, Hq, Sq, _ = q_shape
+    g = torch.Generator().manual_seed(seed)
+    return [tuple(int(torch.randint(hi, (1,), generator=g)) for hi in (B, Hq, Sq)) for _ in range(n)]
+
+
+@torch.no_grad()
+def fp32_row_partials(q, k, v, sel, causal=True, kv_offset=0, seq_kv_total=None):
+    """Softmax statistics of the output rows `sel` over the keys k/v hold (global key
+    positions kv_offset + j of seq_kv_total), in fp32 with plain torch ops on the tensors'
+    device (tests/reference.py's math: scores * head_dim^-0.5, bottom-right causal mask,
+    softmax, @ V; TF32 off). Returns an (n, 2 + D) float64 tensor of rows [m | l | acc]:
+    m the row max of the scores, l = sum exp(s - m), acc = sum exp(s - m) v; a row that
+    sees none of these keys gets (-inf, 0, 0)."""
+    B, Hq, Sq, D = q.shape
+    Hkv, n = k.shape[1], k.shape[2]
+    G = Hq // Hkv
+    total = n if seq_kv_total is None else seq_kv_total
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        out = torch.zeros(len(sel), 2 + D, dtype=torch.float64, device=q.device)
+        pos = torch.arange(n, device=q.device)
+        for r, (b, h, i) in enumerate(sel):
+            s = (k[b, h // G].float() @ q[b, h, i].float()) * D ** -0.5
+            if causal:
+                s = s.masked_fill(pos > i + total - Sq - kv_offset, float("-inf"))
+            m = s.max() if n else torch.tensor(float("-inf"), device=q.device)
+            if not torch.isfinite(m):
+                out[r, 0] = float("-inf")
+                continue
+            p = torch.exp(s - m)
+            out[r, 0], out[r, 1] = m.double(), p.sum().double()
+            out[r, 2:] = (p @ v[b, h // G].float()).double()
+        return out
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+def parity_check(local, world, n_rows=16, sharded_keys=False):
+    """Checks n_rows seeded output rows of this rank against an fp32 torch evaluation of
+    the same rows. With sharded_keys, every rank holds a key range of every row: the
+    ranks' fp32 row statistics are all-gathered and combined (log-sum-exp) before the
+    comparison. The verdict is all-reduced (every rank must pass)."""
+    q, k, v, o = local["q"], local["k"], local["v"], local["o"]
+    sel = check_rows_sel(q.shape, n_rows)
+    part = fp32_row_partials(q, k, v, sel, True, local.get("kv_offset", 0), local.get("seq_kv_total"))
+    if sharded_keys and world > 1:
+        import torch.distributed as dist
+        gathered = [torch.empty_like(part) for _ in range(world)]
+        dist.all_gather(gathered, part)
+        parts = torch.stack(gathered)
+    else:
+        parts = part[None]
+    m = parts[:, :, 0]
+    M = m.max(0).values
+    w = torch.where(torch.isinf(m), torch.zeros_like(m), torch.exp(m - M))
+    ref = (w[:, :, None] * parts[:, :, 2:]).sum(0) / (w * parts[:, :, 1]).sum(0)[:, None]
+    got = torch.stack([o[b, h, i].double() for b, h, i in sel])
+    nan_ok = bool(torch.equal(torch.isnan(ref), torch.isnan(got)))
+    fin = ~torch.isnan(ref)
+    d = (got[fin] - ref[fin]).abs()
+    mx = float(d.max()) if d.numel() else 0.0
+    mn = float(d.mean()) if d.numel() else 0.0
+    ok = nan_ok and mx < CHECK_TOL[0] and mn < CHECK_TOL[1]
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([0.0 if ok else 1.0, mx, mn], dtype=torch.float64, device=q.device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ok, mx, mn = t[0].item() == 0.0, t[1].item(), t[2].item()
+    return {"ok": bool(ok), "rows_per_rank": len(sel), "max_abs": round(mx, 6), "mean_abs": round(mn, 7),
+            "tol": list(CHECK_TOL), "against": "fp32 torch rows (reference math), all ranks"
+            + ("; key shards combined by log-sum-exp" if sharded_keys and world > 1 else "")}
+
+
 # ----------------------------------------------------------------------------- attention arms
 def make_attention(impl):
     """The attention call a step makes: this library (`ours`) or a same-box library
@@ -378,14 +458,22 @@ def run_attention_workload(wl, world, rank, device, steps, warmup, args):
         nb, nh = br[1] - br[0], hr[1] - hr[0]
         q, k, v = rnd(nb, nh * g, Sq, D), rnd(nb, nh, Skv, D), rnd(nb, nh, Skv, D)
 
+        local.update(q=q, k=k, v=v)
+
         def step(i):
             local["o"] = S.head_sharded_forward(q, k, v) if args.impl == "ours" else attn(q, k, v)
         flush = make_flush(device)
         launches_per_step = 1
     elif name == "long_decode":
         k0, k1 = S.kv_range(Skv, world, rank)
+        # q is replicated (seed 0 on every rank); each rank draws its own key shard, one
+        # batch element at a time so the fp32 draw stays small (32 GiB of K/V at N=1)
         q = torch.randn(B, Hq, Sq, D, generator=torch.Generator(device=device).manual_seed(0), device=device).to(dt)
-        k, v = rnd(B, Hkv, k1 - k0, D), rnd(B, Hkv, k1 - k0, D)
+        k = torch.empty(B, Hkv, k1 - k0, D, dtype=dt, device=device)
+        v = torch.empty(B, Hkv, k1 - k0, D, dtype=dt, device=device)
+        for bb in range(B):
+            k[bb], v[bb] = rnd(Hkv, k1 - k0, D), rnd(Hkv, k1 - k0, D)
+        local.update(q=q, k=k, v=v, kv_offset=k0, seq_kv_total=Skv)
         if world == 1:
             def step(i):
                 local["o"] = attn(q, k, v)
@@ -414,6 +502,11 @@ def run_attention_workload(wl, world, rank, device, steps, warmup, args):
     else:
         times, wall = timed_steps(step, steps, warmup, world, device, flush=flush)
     clocks = clock.stop() if clock else None
+    if name == "decode":  # the checked output: one eager step on the first input copy
+        local["q"], local["k"], local["v"] = sets[0]
+        local["o"] = call(0)
+    elif name.startswith("paged"):
+        local.clear()  # paged outputs are checked by the GPU test suite, not in the bench
     mean_ms = statistics.mean(times)
     total_ms = max_over_ranks(sum(times), world, device)
     ms_step = total_ms / steps
@@ -515,45 +608,140 @@ def cpu_threads():
         return 1
 
 
-def cpu_sample(wl, budget_s, steps=None):
-    """Times the oracle port of tests/reference.py on blocks of query rows of the
-    workload (one kv head's query heads at a time). Returns (value, unit, sample text, per-step s)."""
-    from oracle import gqa_oracle as O
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def _sample_blocks(wl, rows):
+    """Row blocks of one (batch, kv head) unit for the CPU samples: (r0, r1, kend) with
+    the key prefix up to the block's last causal bound (keeps the bottom-right offset)."""
+    Sq, Skv = wl["Sq"], wl["Skv"]
+    off = Skv - Sq
+    n = 0
+    while True:
+        r0 = (n * rows * 37) % max(1, Sq - rows + 1) if Sq > rows else 0
+        r1 = min(Sq, r0 + rows)
+        yield r0, r1, min(Skv, r1 + off)
+        n += 1
+
+
+def _sample_work(wl, G, r0, r1, kend):
+    D, Skv = wl["D"], wl["Skv"]
+    pairs = int(np.clip(np.arange(r0, r1) + (Skv - wl["Sq"]) + 1, 0, Skv).sum())
+    kv_elem = 1 if wl.get("kv") == "fp8" else 2  # bytes per cached K/V element of the workload
+    return 4.0 * G * D * pairs, kv_elem * 2 * kend * D + 2.0 * 2 * G * (r1 - r0) * D
+
+
+def cpu_sample(wl, budget_s, steps=None, kind="torch"):
+    """Times the reference's CPU attention on blocks of query rows of the workload (one kv
+    head's query heads at a time). kind "torch": the torch restatement of
+    tests/reference.py (the reference's own torch operations, fp32, every host core);
+    kind "numpy": the numpy port. Returns (value, unit, sample text, per-step s)."""
     B, Hq, Hkv, Sq, Skv, D = wl["B"], wl["Hq"], wl["Hkv"], wl["Sq"], wl["Skv"], wl["D"]
     G = Hq // Hkv
     rng = np.random.default_rng(0)
     rows = Sq if Sq <= 64 else 256  # query rows per sample step
+    from oracle import gqa_oracle as O
     q = rng.standard_normal((1, G, Sq, D), dtype=np.float32)
     k = rng.standard_normal((1, 1, Skv, D), dtype=np.float32)
     v = rng.standard_normal((1, 1, Skv, D), dtype=np.float32)
     q, k, v = (O.bf16_round(x) for x in (q, k, v))
-    done_flops = done_bytes = 0.0
-    elapsed = 0.0
-    n = 0
+    if kind == "torch":
+        from oracle import gqa_oracle_torch as T
+        torch.set_num_threads(host_cores())
+        qt, kt, vt = (torch.from_numpy(x) for x in (q, k, v))
+
+        def run(r0, r1, kend):
+            T.gqa_reference(qt[:, :, r0:r1], kt[:, :, :kend], vt[:, :, :kend], causal=True)
+        what, cores = f"torch {torch.__version__} fp32 restatement of tests/reference.py", torch.get_num_threads()
+    else:
+        def run(r0, r1, kend):
+            O.gqa_reference(q[:, :, r0:r1], k[:, :, :kend], v[:, :, :kend], causal=True)
+        what, cores = "fp32 numpy port of tests/reference.py", cpu_threads()
+    done_flops = done_bytes = elapsed = 0.0
     per = []
-    off = Skv - Sq
-    kv_elem = 1 if wl.get("kv") == "fp8" else 2  # bytes per cached K/V element of the workload
-    while (steps is None and (elapsed < budget_s or n == 0)) or (steps is not None and n < steps):
-        r0 = (n * rows * 37) % max(1, Sq - rows + 1) if Sq > rows else 0
-        r1 = min(Sq, r0 + rows)
-        # rows r0..r1 of one (b, kv head): keys up to the last row's causal bound
-        kend = min(Skv, r1 + off)
+    blocks = _sample_blocks(wl, rows)
+    while (steps is None and (elapsed < budget_s or not per)) or (steps is not None and len(per) < steps):
+        r0, r1, kend = next(blocks)
         t0 = time.perf_counter()
-        O.gqa_reference(q[:, :, r0:r1], k[:, :, :kend], v[:, :, :kend], causal=True)
+        run(r0, r1, kend)
         dt = time.perf_counter() - t0
         per.append(dt)
         elapsed += dt
-        pairs = int(np.clip(np.arange(r0, r1) + off + 1, 0, Skv).sum())
-        done_flops += 4.0 * G * D * pairs
-        done_bytes += kv_elem * 2 * kend * D + 2.0 * 2 * G * (r1 - r0) * D
-        n += 1
+        fl, by = _sample_work(wl, G, r0, r1, kend)
+        done_flops += fl
+        done_bytes += by
     if wl["bound"] == "tensor":
         val, unit = done_flops / elapsed / 1e12, "TFLOP/s"
     else:
         val, unit = done_bytes / elapsed / 1e9, "GB/s"
-    sample = (f"{n} step(s) of {rows} query rows x {G} query heads of one (batch, kv head) unit of the "
-              f"workload, fp32 numpy oracle; {elapsed:.2f} s")
-    return val, unit, sample, per
+    sample = (f"{len(per)} step(s) of {rows} query rows x {G} query heads of one (batch, kv head) unit of the "
+              f"workload, {what}, {cores} threads; {elapsed:.2f} s")
+    return val, unit, sample, per, cores
+
+
+def config_of(wl, world, workload):
+    """The `config` of a bench line; the reference arm prints the same dict."""
+    return {"workload": wl["name"], "batch_per_gpu" if wl["scaling"] == "weak" else "batch": wl["B"],
+            "num_heads": wl["Hq"], "num_kv_heads": wl["Hkv"], "seq_q": wl["Sq"], "seq_kv": wl["Skv"],
+            "head_dim": wl["D"], "causal": True,
+            "l2": "flushed between steps (256 MB write)" if workload in ("prefill", "chunked")
+            else "inputs larger than L2 (4 rotating copies, 268 MB); 16-step CUDA graphs back to back"
+            if workload == "decode"
+            else "inputs larger than L2 (2 rotating caches); 16-step CUDA graphs back to back"
+            if workload.startswith("paged")
+            else "inputs larger than L2 (32 GiB K/V)",
+            "parallelism": (f"batch-sharded x{world}" if wl["scaling"] == "weak" else
+                            f"kv-head/batch x{world}" if workload == "chunked" else
+                            f"seq_kv x{world} + NCCL all-gather LSE combine")}
+
+
+def roofline_of(wl, res, world, peaks, workload):
+    """Roofline of the dominant kernel from rank 0's mean per-step event time. Per-rank
+    work: one workload instance (weak scaling) or 1/world of it (strong scaling)."""
+    launch_ms = res["mean_ms_rank0"]
+    share = 1.0 if wl["scaling"] == "weak" else 1.0 / world
+    if wl["bound"] == "tensor":
+        work = attn_flops(wl["B"], wl["Hq"], wl["Sq"], wl["Skv"], wl["D"]) * share
+        achieved = work / (launch_ms * 1e-3) / 1e12
+        return {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16"], "unit": "TFLOP/s",
+                "frac": round(achieved / peaks["bf16"], 4),
+                "frac_of_sustained": round(achieved / peaks["bf16_sus"], 4) if peaks["bf16_sus"] else None,
+                "peak_source": f"{peaks['source']} bf16 dense burst (MEASURED_PEAKS.json)",
+                "work_per_launch": work, "traffic": profile_traffic(workload)}
+    work = wl_bytes(wl) * share
+    achieved = work / (launch_ms * 1e-3) / 1e9
+    return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm"], "unit": "GB/s",
+            "frac": round(achieved / peaks["hbm"], 4),
+            "peak_source": f"{peaks['source']} HBM copy (MEASURED_PEAKS.json)",
+            "work_per_launch": work, "traffic": profile_traffic(workload)}
+
+
+def sharded_object(key, args, world, rank, device, peaks, comparator):
+    """One of the sharded configurations of the default line (config 4 or 5) at this N:
+    timed like its standalone workload, then checked row by row."""
+    wname, nsteps = {"chunked_b4": ("chunked", args.chunked_steps),
+                     "long_decode": ("long_decode", args.long_steps)}[key]
+    swl = WORKLOADS[wname]
+    sargs = argparse.Namespace(**{**vars(args), "workload": wname})
+    res = run_attention_workload(swl, world, rank, device, nsteps, args.warmup, sargs)
+    par = parity_check(res["local"], world, sharded_keys=(wname == "long_decode"))
+    res["local"].clear()
+    torch.cuda.empty_cache()
+    peak = peaks["bf16"] if swl["bound"] == "tensor" else peaks["hbm"]
+    obj = {"value": round(res["value"], 3), "unit": res["unit"], "ms_per_step": round(res["ms_per_step"], 5),
+           "steps": nsteps, "scaling": swl["scaling"], "n_gpus": world,
+           "frac_of_n_peak": round(res["value"] / (world * peak), 4),
+           "config": config_of(swl, world, wname), "roofline": roofline_of(swl, res, world, peaks, wname),
+           "parity": par, "clocks": res["clocks"]}
+    if world > 1:
+        import torch.distributed as dist
+        obj["nccl"] = {"backend": dist.get_backend(), "ranks": dist.get_world_size(),
+                       "collectives_per_step": 1 if wname == "long_decode" else 0}
+    return obj, (0 if comparator else res["launches"])
 
 
 # ----------------------------------------------------------------------------- main
@@ -568,7 +756,11 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode half of the default line")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="skip the sharded configurations (4 and 5) of the default line")
     ap.add_argument("--decode-steps", type=int, default=5000, help="timed steps of the decode half")
+    ap.add_argument("--chunked-steps", type=int, default=200, help="timed steps of the config-4 object")
+    ap.add_argument("--long-steps", type=int, default=40, help="timed steps of the config-5 object")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -610,41 +802,14 @@ def main():
         "vs_baseline": None,
         "dtype": "e4m3 K/V, f16 MMA, bf16 Q/O" if wl.get("kv") == "fp8" else "bf16",
         "data": "synthetic (N(0,1) bf16, CUDA generator seeded by rank)",
-        "config": {"workload": wl["name"], "batch_per_gpu" if wl["scaling"] == "weak" else "batch": wl["B"],
-                   "num_heads": wl["Hq"], "num_kv_heads": wl["Hkv"], "seq_q": wl["Sq"], "seq_kv": wl["Skv"],
-                   "head_dim": wl["D"], "causal": True,
-                   "l2": "flushed between steps (256 MB write)" if args.workload in ("prefill", "chunked")
-                   else "inputs larger than L2 (4 rotating copies, 268 MB); 16-step CUDA graphs back to back"
-                   if args.workload == "decode"
-                   else "inputs larger than L2 (2 rotating caches); 16-step CUDA graphs back to back"
-                   if args.workload.startswith("paged")
-                   else "inputs larger than L2 (32 GiB K/V)",
-                   "parallelism": (f"batch-sharded x{world}" if wl["scaling"] == "weak" else
-                                   f"kv-head/batch x{world}" if args.workload == "chunked" else
-                                   f"seq_kv x{world} + NCCL all-gather LSE combine")},
+        "config": config_of(wl, world, args.workload),
         "gpu_launches": 0 if comparator else res["launches"],
     }
-    # roofline of the dominant kernel, from rank 0's mean per-launch event time. Per-rank
-    # work: one workload instance (weak scaling) or 1/world of it (strong scaling).
-    launch_ms = res["mean_ms_rank0"]
-    share = 1.0 if wl["scaling"] == "weak" else 1.0 / world
-    if wl["bound"] == "tensor":
-        work = attn_flops(wl["B"], wl["Hq"], wl["Sq"], wl["Skv"], wl["D"]) * share
-        achieved = work / (launch_ms * 1e-3) / 1e12
-        line["roofline"] = {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16"],
-                            "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16"], 4),
-                            "frac_of_sustained": (round(achieved / peaks["bf16_sus"], 4)
-                                                  if peaks["bf16_sus"] else None),
-                            "peak_source": f"{peaks['source']} bf16 dense burst (MEASURED_PEAKS.json)",
-                            "work_per_launch": work, "traffic": profile_traffic(args.workload)}
-    else:
-        work = wl_bytes(wl) * share
-        achieved = work / (launch_ms * 1e-3) / 1e9
-        line["roofline"] = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm"], "unit": "GB/s",
-                            "frac": round(achieved / peaks["hbm"], 4),
-                            "peak_source": f"{peaks['source']} HBM copy (MEASURED_PEAKS.json)",
-                            "work_per_launch": work, "traffic": profile_traffic(args.workload)}
+    line["roofline"] = roofline_of(wl, res, world, peaks, args.workload)
     line["clocks"] = res["clocks"]
+    if res["local"]:
+        line["parity"] = parity_check(res["local"], world, sharded_keys=(args.workload == "long_decode"))
+    res["local"].clear()
 
     # decode half of the headline metric
     if args.workload == "prefill" and not args.no_decode:
@@ -662,8 +827,20 @@ def main():
                                            "peak": peaks["hbm"], "unit": "GB/s",
                                            "frac": round(dbytes / (dl_ms * 1e-3) / 1e9 / peaks["hbm"], 4),
                                            "traffic": profile_traffic("decode")},
+                              "parity": parity_check(dres["local"], world),
                               "clocks": dres["clocks"]}
+        dres["local"].clear()
         line["gpu_launches"] += 0 if comparator else dres["launches"]
+
+    # the sharded configurations (BASELINE configs 4 and 5), strong-scaled over the N ranks
+    if args.workload == "prefill" and not args.no_sharded:
+        for key in ("chunked_b4", "long_decode"):
+            if comparator and key == "long_decode" and world > 1:
+                continue  # the library comparators have no key-sharded path
+            torch.cuda.empty_cache()
+            obj, launches = sharded_object(key, args, world, rank, device, peaks, comparator)
+            line[key] = obj
+            line["gpu_launches"] += launches
 
     if not args.no_e2e:
         e2e = run_e2e(wl, world, rank, device, 20 if args.workload == "prefill" else 200, args)
@@ -671,9 +848,12 @@ def main():
             line["e2e"] = e2e
 
     if rank == 0 and world == 1 and not args.no_cpu:
-        val, unit, sample, _ = cpu_sample(wl, budget_s=12.0)
-        line["cpu_baseline"] = {"value": round(val, 5), "unit": unit, "cores": cpu_threads(), "kind": "port",
-                                "sample": sample}
+        val, unit, sample, _, cores = cpu_sample(wl, budget_s=10.0, kind="torch")
+        nval, nunit, nsample, _, ncores = cpu_sample(wl, budget_s=4.0, kind="numpy")
+        line["cpu_baseline"] = {"value": round(val, 5), "unit": unit, "cores": cores, "kind": "port",
+                                "sample": sample,
+                                "numpy_port": {"value": round(nval, 5), "unit": nunit, "cores": ncores,
+                                               "sample": nsample}}
 
     if world > 1:
         import torch.distributed as dist
@@ -688,26 +868,27 @@ def main():
 
 
 def main_reference(args, wl, steps):
-    """The reference arm: the reference's CPU path (numpy port of tests/reference.py)."""
+    """The reference arm: the reference's CPU path, its torch attention
+    (tests/reference.py, restated in oracle/gqa_oracle_torch.py) in fp32 on every host core."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
     # each step is one block of query rows; run as many of the requested warmup + steps
     # as fit in about two minutes (at least 3)
-    _, _, _, per = cpu_sample(wl, budget_s=0.0, steps=1)
+    _, _, _, per, _ = cpu_sample(wl, budget_s=0.0, steps=1, kind="torch")
     total = steps + args.warmup
     n_run = max(3, min(total, int(120.0 / max(per[0], 1e-3))))
-    val, unit, sample, per = cpu_sample(wl, budget_s=0.0, steps=n_run)
+    val, unit, sample, per, cores = cpu_sample(wl, budget_s=0.0, steps=n_run, kind="torch")
     ms_step = statistics.mean(per) * 1e3
     line = {
         "metric": METRIC if args.workload in ("prefill", "decode") else f"{args.workload} {unit}",
         "value": round(val, 6), "unit": unit, "impl": "reference", "n_gpus": world, "steps": steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 3), "higher_is_better": True,
-        "scaling": wl["scaling"], "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": wl["name"], "num_heads": wl["Hq"], "num_kv_heads": wl["Hkv"], "seq_q": wl["Sq"],
-                   "seq_kv": wl["Skv"], "head_dim": wl["D"], "causal": True},
-        "cpu_baseline": {"value": round(val, 6), "unit": unit, "cores": cpu_threads(), "kind": "port",
+        "scaling": wl["scaling"], "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (N(0,1) bf16-rounded, numpy generator seeded 0)",
+        "config": config_of(wl, world, args.workload),
+        "cpu_baseline": {"value": round(val, 6), "unit": unit, "cores": cores, "kind": "port",
                          "sample": sample + f"; {n_run} of {total} requested steps run (bounded)"},
         "e2e": {"value": round(val, 6), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }

@@ -75,4 +75,18 @@ __global__ void gqa_fill_nan_kernel(uint16_t* o, int64_t o_sb, int64_t o_sh, int
   }
 }
 
+// The partial of an empty key range: m = -inf, l = 0, acc = 0 for every row (rows
+// m/l, rows x head_dim acc, contiguous). A rank whose key shard holds no key
+// contributes it; the combine gives it weight exp2(-inf - M) = 0.
+__global__ void gqa_fill_empty_partial_kernel(float* m, float* l, float* acc, int64_t rows, int head_dim) {
+  const int64_t n = rows * head_dim;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    acc[i] = 0.f;
+    if (i < rows) {
+      m[i] = -INFINITY;
+      l[i] = 0.f;
+    }
+  }
+}
+
 }  // namespace gqa

@@ -38,6 +38,25 @@ __device__ __forceinline__ void report_device_error(int code, int site) {
   if (atomicCAS(&g_device_error, 0, code) == 0) g_device_error_site = site;
 }
 
+#ifdef GQA_DEBUG_CHECKS
+// Test hooks of the checked build (gqa_debug_inject): the wait limit can be
+// shortened at run time, and the TMA producer of one CTA can withhold one of its
+// loads (no expect-tx, no copy), so the consumer's bounded wait on that load runs
+// out and the abort path runs -- no memory is touched that a release build would
+// not touch, and nothing is left in flight. Release builds compile these to
+// constants.
+__device__ unsigned long long g_wait_limit_ns = kWaitLimitNs;
+__device__ int g_withhold_cta = -1;
+__device__ int g_withhold_load = -1;
+__device__ __forceinline__ uint64_t wait_limit_ns() { return g_wait_limit_ns; }
+__device__ __forceinline__ bool withheld_load(int t) {
+  return (int)blockIdx.x == g_withhold_cta && t == g_withhold_load;
+}
+#else
+__device__ __forceinline__ uint64_t wait_limit_ns() { return kWaitLimitNs; }
+__device__ __forceinline__ bool withheld_load(int) { return false; }
+#endif
+
 // Debug builds (-DGQA_DEBUG_CHECKS, `build.py --debug`): the TMA, UMMA and TMEM
 // helpers below check their addresses and coordinates first. A failed check records
 // GQA_ERR_DEBUG_CHECK and a site id in the device error word and skips the access;
@@ -112,7 +131,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     for (int i = 0; i < 4; ++i)
       if (mbar_try_wait_suspend(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > wait_limit_ns()) {
       *abort_flag = 1;
       report_device_error(GQA_ERR_TIMEOUT, site);
       return false;
@@ -147,6 +166,17 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
       " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
+}
+// L2 prefetch of one tensor-map box (no shared-memory destination, no barrier). A
+// hint only: the line is fetched into L2 and later loads read it through L2, which
+// any write to it also goes through, so it may be issued before the grid dependency
+// wait without changing what the kernel reads.
+__device__ __forceinline__ void tma_prefetch_l2_4d(const CUtensorMap* map, int c0, int c1, int c2, int c3) {
+  if (!GQA_CHECK((c0 & 7) == 0, 905)) return;
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
 }
 __device__ __forceinline__ void tma_load_4d_hint(uint32_t dst, const CUtensorMap* map, uint32_t bar,
                                                  int c0, int c1, int c2, int c3, uint64_t policy) {
@@ -408,8 +438,9 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
 // pipes share the softmax's exponentials. Cody-Waite style range reduction:
 // n = round(x) through the 1.5 * 2^23 addend (n lands in the low mantissa bits
 // of t), f = x - n in [-1/2, 1/2]; 2^f by a degree-3 polynomial fitted for
-// near-equioscillating relative error (csrc/fit_exp2.py; max relative error
-// 1.5e-4, far below the 2^-8 step of the bf16 P it feeds); the result's
+// near-equioscillating relative error (tests/exp2_fit.py, which a CPU test binds
+// to these constants; max relative error 1.5e-4, far below the 2^-8 step of the
+// bf16 P it feeds); the result's
 // exponent field then gets n added. x is clamped at -126 so the exponent never
 // underflows into the sign bit: x < -126 (masked keys, -inf) gives about 1e-38
 // instead of 0, negligible against any visible key; a NaN x (row with no visible

@@ -271,6 +271,7 @@ __global__ void __launch_bounds__(384, 1)
           }
         }
         if (use > 0 && !mbar_wait(bar_kv_empty + 8 * slot, (use - 1) & 1, abort_flag, 1)) break;
+        if (withheld_load(t)) continue;
         const uint32_t full = bar_kv_full + 8 * slot;
         mbar_arrive_expect_tx(full, Cfg::kTileBytes);
         const CUtensorMap* map = (t & 1) ? &vmap : &kmap;
@@ -294,7 +295,7 @@ __global__ void __launch_bounds__(384, 1)
       if (t < n_loads) {  // aborted: let in-flight loads land before teardown
         volatile int dummy = 0;
         for (int u = max(0, t - SLOTS); u < t; ++u)
-          mbar_wait(bar_kv_full + 8 * (u % SLOTS), (u / SLOTS) & 1, &dummy, 2);
+          if (!withheld_load(u)) mbar_wait(bar_kv_full + 8 * (u % SLOTS), (u / SLOTS) & 1, &dummy, 2);
       }
     }
   } else if (warp == 8) {

@@ -901,12 +901,21 @@ int gqa_partial(const void* q, const void* k, const void* v, float* m_out, float
   if (kv_offset < 0 || seq_kv_total < kv_offset + seq_kv_local) return GQA_ERR_INVALID_ARG;
   if (batch == 0 || seq_q == 0) return GQA_OK;
   if (s.group > kStreamMaxRows) return GQA_ERR_UNSUPPORTED;
-  if (seq_kv_local == 0) return GQA_ERR_INVALID_ARG;
-  rc = check_common(q, k, v, qs, ks, vs, dtype);
-  if (rc) return rc;
+  if (dtype != GQA_DTYPE_BF16 && dtype != GQA_DTYPE_F16) return GQA_ERR_UNSUPPORTED;
   if (!aligned16(acc_out)) return GQA_ERR_ALIGNMENT;
   int sm = 0;
   rc = current_device(&sm);
+  if (rc) return rc;
+  if (seq_kv_local == 0) {
+    // An empty shard (more ranks than 64-key blocks) is a valid part: (-inf, 0, 0)
+    // for every row, which the combine weighs 0. k and v may have no storage.
+    const int64_t rows = (int64_t)batch * num_heads * seq_q;
+    const int blocks = (int)std::min<int64_t>((rows * head_dim + 255) / 256, 4096);
+    gqa_fill_empty_partial_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(m_out, l_out, acc_out,
+                                                                                           rows, head_dim);
+    return launch_status();
+  }
+  rc = check_common(q, k, v, qs, ks, vs, dtype);
   if (rc) return rc;
   const StreamPlan pl = plan_stream(s, sm, true);
   if (!workspace || workspace_bytes < stream_ws_bytes(pl, head_dim) || !aligned16(workspace))
@@ -934,6 +943,52 @@ int gqa_lse_combine(const float* m_parts, const float* l_parts, const float* acc
                          acc_part_stride, 1};
   return gqa_split_reduce(m_parts, l_parts, acc_parts, o, ps, as, os, batch, num_heads, seq_q, head_dim, nparts,
                           dtype, stream);
+}
+
+#ifdef GQA_DEBUG_CHECKS
+namespace gqa {
+__global__ void gqa_exp2_poly2_kernel(const float* x, float* y, int n) {
+  const int i = 2 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (i + 1 < n) {
+    const float2 r = exp2_poly2(make_float2(x[i], x[i + 1]));
+    y[i] = r.x;
+    y[i + 1] = r.y;
+  } else if (i < n) {
+    y[i] = exp2_poly2(make_float2(x[i], x[i])).x;
+  }
+}
+}  // namespace gqa
+#endif
+
+int gqa_debug_inject(int cta, int load, long long wait_limit_ns) {
+#ifdef GQA_DEBUG_CHECKS
+  const int rc = current_device(nullptr);
+  if (rc) return rc;
+  const unsigned long long lim = wait_limit_ns > 0 ? (unsigned long long)wait_limit_ns : kWaitLimitNs;
+  if (cudaMemcpyToSymbol(g_withhold_cta, &cta, sizeof(int)) != cudaSuccess) return GQA_ERR_CUDA;
+  if (cudaMemcpyToSymbol(g_withhold_load, &load, sizeof(int)) != cudaSuccess) return GQA_ERR_CUDA;
+  if (cudaMemcpyToSymbol(g_wait_limit_ns, &lim, sizeof(lim)) != cudaSuccess) return GQA_ERR_CUDA;
+  return GQA_OK;
+#else
+  (void)cta; (void)load; (void)wait_limit_ns;
+  return GQA_ERR_UNSUPPORTED;
+#endif
+}
+
+int gqa_debug_exp2_poly2(const float* x, float* y, int n, void* stream) {
+#ifdef GQA_DEBUG_CHECKS
+  if (!x || !y || n < 0) return GQA_ERR_INVALID_ARG;
+  const int rc = current_device(nullptr);
+  if (rc) return rc;
+  if (n == 0) return GQA_OK;
+  const int threads = 256, pairs = (n + 1) / 2;
+  gqa_exp2_poly2_kernel<<<(pairs + threads - 1) / threads, threads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      x, y, n);
+  return launch_status();
+#else
+  (void)x; (void)y; (void)n; (void)stream;
+  return GQA_ERR_UNSUPPORTED;
+#endif
 }
 
 int gqa_device_error(int* code, int* site, int clear) {

@@ -82,6 +82,9 @@ struct StreamCfg {
   static constexpr int kStageBytes = 2 * kTileBytes;
   static constexpr int kStages = (HD == 128) ? 3 : 6;
   static constexpr int kRingBytes = kStages * kStageBytes;  // 192 KB: one CTA per SM
+  // K+V bytes of its chunk a CTA prefetches into L2 before the grid dependency wait:
+  // 148 resident CTAs x 512 KB = 76 MB, within the 126 MB L2.
+  static constexpr int kPrefetchBytes = 512 * 1024;
   static constexpr int kWarps = 8;                          // compute warps
   static constexpr int kThreads = (kWarps + 1) * 32;        // + one TMA producer warp
   // barriers (full[kStages], empty[kStages], combine) + flags after the ring
@@ -158,6 +161,26 @@ __global__ void __launch_bounds__(288, 1)
     tma_prefetch_desc(&kmap);
     tma_prefetch_desc(&vmap);
   }
+  // Dense K/V: the chunk's key range follows from the parameters alone, so the
+  // producer warp asks for the first kPrefetchBytes of it in L2 before the grid
+  // dependency wait. Under programmatic dependent launch this CTA becomes resident
+  // as soon as a CTA of the previous grid leaves its SM, so these reads overlap the
+  // previous grid's tail (its cross-warp merge, publish and combine), when HBM would
+  // otherwise idle. The prefetch is a hint (the loads after the wait still read
+  // through L2), so it cannot return stale data even if the previous grid writes
+  // K or V. Paged calls skip it: their block table may be written by that grid.
+  if (!paged && warp == NW) {
+    int kv_end0 = p.seq_kv;
+    if (p.causal) kv_end0 = min(kv_end0, min((mt + 1) * p.block_m, p.seq_q) - 1 + off - p.kv_offset + 1);
+    const int kb = split * p.chunk;
+    const int ke = min(min(kb + p.chunk, kv_end0), kb + Cfg::kPrefetchBytes / (Cfg::kStageBytes / Cfg::kBN));
+    const int nbox = (ke > kb) ? (ke - kb + Cfg::kBox - 1) / Cfg::kBox : 0;
+    for (int i = lane; i < nbox * Cfg::kNSub; i += 32) {
+      const int key = kb + (i / Cfg::kNSub) * Cfg::kBox, c0 = (i % Cfg::kNSub) * 64;
+      tma_prefetch_l2_4d(&kmap, c0, key, kvh, b);
+      tma_prefetch_l2_4d(&vmap, c0, key, kvh, b);
+    }
+  }
   pdl_wait();
 
   // Highest key (local, exclusive) any valid row of this unit may see.
@@ -215,7 +238,7 @@ __global__ void __launch_bounds__(288, 1)
       if (t < n_first) stage_blocks(t, pb[t][0], pb[t][1]);
 #pragma unroll
     for (int t = 0; t < Cfg::kStages; ++t)
-      if (t < n_first) issue(t, pb[t][0], pb[t][1]);
+      if (t < n_first && !withheld_load(t)) issue(t, pb[t][0], pb[t][1]);
   }
   pdl_trigger();
   __syncthreads();
@@ -229,13 +252,13 @@ __global__ void __launch_bounds__(288, 1)
         int pb0, pb1;
         stage_blocks(t, pb0, pb1);
         if (!mbar_wait(bar_empty + 8 * slot, (t / Cfg::kStages - 1) & 1, abort_flag, 101)) break;
-        issue(t, pb0, pb1);
+        if (!withheld_load(t)) issue(t, pb0, pb1);
       }
       // On abort, let the loads already issued land before the CTA exits.
       if (t < n_stages) {
         for (int u = max(0, t - Cfg::kStages); u < t; ++u) {
           volatile int dummy = 0;
-          mbar_wait(bar_full + 8 * (u % Cfg::kStages), (u / Cfg::kStages) & 1, &dummy, 102);
+          if (!withheld_load(u)) mbar_wait(bar_full + 8 * (u % Cfg::kStages), (u / Cfg::kStages) & 1, &dummy, 102);
         }
       }
     }
@@ -791,7 +814,11 @@ __global__ void __launch_bounds__(288, 1)
     }
   }
   GQA_CBAR();
-  if (staged) mbar_wait(bar_comb, 0, abort_flag, 104);
+  if (staged) {
+    // Waited for even after an abort: the bulk copy must land before the CTA exits.
+    volatile int no_abort = 0;
+    mbar_wait(bar_comb, 0, &no_abort, 104);
+  }
   for (int idx = tid; idx < n_rows * per_row; idx += CT) {
     const int r = idx / per_row, d = (idx - r * per_row) * 4;
     const int g = r / p.block_m, m = r - g * p.block_m, pos = mt * p.block_m + m;

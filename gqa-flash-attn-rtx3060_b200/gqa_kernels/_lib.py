@@ -56,6 +56,8 @@ SIGNATURES = {
     "gqa_prefill_plan": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, ctypes.POINTER(ctypes.c_int)]),
     "gqa_paged_fwd_kv8": (_I, [_P, _P, _P, _P, _I64P, _I64P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _F,
                                _F, _I, _I, _P, _SZ, _P]),
+    "gqa_debug_inject": (_I, [_I, _I, ctypes.c_longlong]),
+    "gqa_debug_exp2_poly2": (_I, [_P, _P, _I, _P]),
 }
 
 _lib = None
@@ -167,8 +169,15 @@ WORKSPACES = WorkspaceCache()
 
 
 def device_error(clear=True):
-    """Returns (code, site) of the current device's in-kernel error word."""
+    """Returns (code, site) of the current device's in-kernel error word.
+
+    A nonzero code means some launch aborted (a bounded wait expired, or a checked
+    build's check failed). The split kernels' ticket counters in a cached workspace
+    are then no longer trusted: the device's cached workspaces are dropped, so the
+    next call allocates zeroed ones."""
     code = ctypes.c_int(0)
     site = ctypes.c_int(0)
     check(load().gqa_device_error(ctypes.byref(code), ctypes.byref(site), 1 if clear else 0), "gqa_device_error")
+    if code.value != 0:
+        WORKSPACES.drop(torch.device("cuda", torch.cuda.current_device()))
     return code.value, site.value

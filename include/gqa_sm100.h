@@ -136,7 +136,9 @@ int gqa_split_fused_noalloc(const void* q, const void* k, const void* v, void* o
  * sequence of seq_kv_total keys; causal masking uses global key positions.
  * Outputs are float32, contiguous: m_out/l_out (batch, num_heads, seq_q),
  * acc_out (batch, num_heads, seq_q, head_dim), with the meaning of
- * gqa_split_first's (m, l, acc) for this shard.
+ * gqa_split_first's (m, l, acc) for this shard. seq_kv_local may be 0 (a rank
+ * whose share of the keys is empty): the outputs are then (-inf, 0, 0) for every
+ * row, which gqa_lse_combine weighs 0, and k/v are not read.
  * No reference counterpart (the reference is single-GPU); the partial
  * definition follows gqa_kernels/gqa_split.py:102-112.
  */
@@ -249,6 +251,25 @@ int gqa_device_error(int* code, int* site, int clear);
 
 /* Number of SMs of the current device as used for split sizing. */
 int gqa_sm_count(void);
+
+/*
+ * Test hooks of the checked build (libgqa_sm100_debug.so, build.py --debug); the
+ * release library returns GQA_ERR_UNSUPPORTED from both. No reference counterpart:
+ * they exist to test this library's failure detection and arithmetic on the GPU.
+ *
+ * gqa_debug_inject: the TMA producer of CTA `cta` withholds its load number `load`
+ * (prefill: the K/V tile load index, K and V alternating; streaming kernel: the
+ * stage index) in every following launch, and every bounded in-kernel wait gives up
+ * after wait_limit_ns (<= 0 restores the default). The consumer's wait on the
+ * withheld load then expires: the kernel records GQA_ERR_TIMEOUT in the device error
+ * word, aborts the CTA (its other waits end, issued copies land, TMEM is freed) and
+ * returns. cta = -1 withholds nothing. Applies to the current device.
+ *
+ * gqa_debug_exp2_poly2: y[i] = the kernels' FMA-pipe exp2 (the polynomial the prefill
+ * softmax uses for one column pair in eight) of x[i], for i < n; device pointers.
+ */
+int gqa_debug_inject(int cta, int load, long long wait_limit_ns);
+int gqa_debug_exp2_poly2(const float* x, float* y, int n, void* stream);
 
 #ifdef __cplusplus
 }

@@ -283,6 +283,11 @@ def partial_attention(q, k_shard, v_shard, causal, kv_offset, seq_kv_total, dtyp
     m = np.empty((B, Hq, Sq), dtype=dtype)
     l = np.empty((B, Hq, Sq), dtype=dtype)
     acc = np.empty((B, Hq, Sq, D), dtype=dtype)
+    if n == 0:  # an empty shard: every row sees none of its keys
+        m.fill(-np.inf)
+        l.fill(0.0)
+        acc.fill(0.0)
+        return m, l, acc
     keys = kv_offset + np.arange(n)
     for b in range(B):
         for h in range(Hq):

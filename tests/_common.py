@@ -44,30 +44,10 @@ def compare(out, ref, tol, allow_nan_rows=True):
     return mx, mn
 
 
-@torch.no_grad()
 def torch_reference(q, k, v, causal=True, row_block=2048):
     """tests/reference.py semantics in fp32 on the tensors' device, chunked over
-    (batch, kv head, query rows) so the score matrix stays bounded. TF32 off."""
-    prev = torch.backends.cuda.matmul.allow_tf32
-    torch.backends.cuda.matmul.allow_tf32 = False
-    try:
-        B, Hq, Sq, D = q.shape
-        _, Hkv, Skv, _ = k.shape
-        G = Hq // Hkv
-        out = torch.empty(q.shape, dtype=torch.float32, device=q.device)
-        kpos = torch.arange(Skv, device=q.device)
-        for b in range(B):
-            for kv in range(Hkv):
-                kf = k[b, kv].float()
-                vf = v[b, kv].float()
-                for r0 in range(0, Sq, row_block):
-                    r1 = min(Sq, r0 + row_block)
-                    qs = q[b, kv * G:(kv + 1) * G, r0:r1].float()
-                    s = torch.matmul(qs, kf.T) * (D ** -0.5)
-                    if causal:
-                        qpos = torch.arange(r0, r1, device=q.device) + (Skv - Sq)
-                        s = s.masked_fill(qpos[:, None] < kpos[None, :], float("-inf"))
-                    out[b, kv * G:(kv + 1) * G, r0:r1] = torch.matmul(torch.softmax(s, dim=-1), vf)
-        return out
-    finally:
-        torch.backends.cuda.matmul.allow_tf32 = prev
+    (batch, kv head, query rows) so the score matrix stays bounded. TF32 off.
+    The torch restatement of the reference oracle, pinned to the reference's
+    fixtures by tests/test_oracle_golden.py."""
+    from oracle.gqa_oracle_torch import gqa_reference_blocked
+    return gqa_reference_blocked(q, k, v, causal=causal, row_block=row_block)

@@ -7,7 +7,9 @@ squares on a Chebyshev grid. The evaluation below mirrors the kernel's float32
 instruction sequence (round-to-nearest via the 1.5 * 2^23 addend, Horner FMAs,
 exponent add on the bit pattern) and reports its error against numpy.exp2.
 
-    python gqa-flash-attn-rtx3060_b200/csrc/fit_exp2.py
+    python tests/exp2_fit.py
+
+tests/test_exp2_fit_host.py checks that the kernel's coefficients are this fit.
 """
 import numpy as np
 

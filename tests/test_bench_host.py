@@ -43,7 +43,86 @@ def test_causal_pairs_edge_cases(bench):
 
 
 def test_cpu_sample_is_bounded_and_counts_its_work(bench):
-    val, unit, sample, per = bench.cpu_sample(bench.WORKLOADS["decode"], budget_s=0.0, steps=2)
-    assert unit == "GB/s" and val > 0 and len(per) == 2 and "2 step(s)" in sample
-    val, unit, _, _ = bench.cpu_sample(bench.WORKLOADS["paged_decode_fp8"], budget_s=0.0, steps=1)
-    assert unit == "GB/s" and val > 0
+    for kind in ("torch", "numpy"):
+        val, unit, sample, per, cores = bench.cpu_sample(bench.WORKLOADS["decode"], budget_s=0.0, steps=2, kind=kind)
+        assert unit == "GB/s" and val > 0 and len(per) == 2 and "2 step(s)" in sample and cores >= 1
+        val, unit, _, _, _ = bench.cpu_sample(bench.WORKLOADS["paged_decode_fp8"], budget_s=0.0, steps=1, kind=kind)
+        assert unit == "GB/s" and val > 0
+    val, unit, sample, _, _ = bench.cpu_sample(bench.WORKLOADS["prefill"], budget_s=0.0, steps=1, kind="torch")
+    assert unit == "TFLOP/s" and "tests/reference.py" in sample
+
+
+def test_reference_arm_config_is_the_gpu_line_config(bench):
+    """The reference arm prints the config dict of the GPU line (same workload, same N)."""
+    for name, wl in bench.WORKLOADS.items():
+        for world in (1, 8):
+            a = bench.config_of(wl, world, name)
+            assert a == bench.config_of(dict(wl), world, name)
+            assert a["workload"] == wl["name"] and a["seq_kv"] == wl["Skv"]
+
+
+def _rows_setup(seed=0, B=2, Hq=8, Hkv=2, Sq=5, Skv=300, D=64):
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, Hq, Sq, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, Hkv, Skv, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, Hkv, Skv, D, generator=g).to(torch.bfloat16)
+    return q, k, v
+
+
+def test_parity_check_accepts_the_oracle_and_rejects_a_planted_error(bench):
+    import torch
+    from oracle import gqa_oracle_torch as T
+    q, k, v = _rows_setup()
+    o = T.gqa_reference_blocked(q, k, v, causal=True).to(torch.bfloat16)
+    assert bench.parity_check({"q": q, "k": k, "v": v, "o": o}, 1)["ok"]
+    bad = o.clone()
+    for b, h, i in bench.check_rows_sel(q.shape, 16)[:1]:
+        bad[b, h, i, 3] += 0.25  # one wrong element in one checked row
+    res = bench.parity_check({"q": q, "k": k, "v": v, "o": bad}, 1)
+    assert not res["ok"] and res["max_abs"] >= 0.2
+
+
+def test_row_partials_combine_to_the_full_rows(bench):
+    """Key-range statistics of the in-run check, combined by log-sum-exp, equal the rows
+    over all keys (the check of the key-sharded configuration), empty ranges included."""
+    import torch
+    q, k, v = _rows_setup(seed=1)
+    sel = bench.check_rows_sel(q.shape, 12, seed=3)
+    full = bench.fp32_row_partials(q, k, v, sel)
+    ref = full[:, 2:] / full[:, 1:2]
+    for cuts in ([0, 100, 300], [0, 0, 64, 300], [0, 299, 300, 300]):
+        parts = torch.stack([bench.fp32_row_partials(q, k[:, :, a:b], v[:, :, a:b], sel, True, a, 300)
+                             for a, b in zip(cuts, cuts[1:])])
+        m = parts[:, :, 0]
+        w = torch.where(torch.isinf(m), torch.zeros_like(m), torch.exp(m - m.max(0).values))
+        got = (w[:, :, None] * parts[:, :, 2:]).sum(0) / (w * parts[:, :, 1]).sum(0)[:, None]
+        assert torch.allclose(got, ref, rtol=1e-6, atol=1e-7)
+
+
+def _sharded_parity_rank(rank, world):
+    import importlib.util
+    import torch
+    from oracle import gqa_oracle_torch as T
+    spec = importlib.util.spec_from_file_location("bench_rank", os.path.join(ROOT, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    q, k, v = _rows_setup(seed=2, Skv=400)
+    o = T.gqa_reference_blocked(q, k, v, causal=True).to(torch.bfloat16)
+    a, b = (0, 128) if rank == 0 else (128, 400)
+    local = {"q": q, "k": k[:, :, a:b], "v": v[:, :, a:b], "o": o, "kv_offset": a, "seq_kv_total": 400}
+    good = bench.parity_check(local, world, sharded_keys=True)["ok"]
+    # a wrong output on one rank fails the check on every rank
+    if rank == 1:
+        local["o"] = o + 0.5
+    bad = bench.parity_check(local, world, sharded_keys=True)["ok"]
+    return good, bad
+
+
+def test_sharded_parity_check_over_gloo():
+    from tests._dist import run_ranks
+    out = run_ranks(_sharded_parity_rank, 2, timeout_s=60)
+    assert len(out) == 2, out
+    for rank, (status, res) in out.items():
+        assert status == "ok", res
+        assert res == (True, False), (rank, res)

@@ -51,3 +51,30 @@ def test_peer_exception_is_reported():
     assert res[0][0] == "error" and "injected" in res[0][1]
     status, val = res[1]
     assert status == "error" or val[0] == "raised", res[1]
+
+
+def test_device_error_drops_cached_workspaces(monkeypatch):
+    """A nonzero device error word (an aborted launch) makes the split kernels' cached
+    workspaces untrusted: reading it drops them, so the next call starts from zeroed
+    ticket counters. A fake library stands in for the GPU."""
+    import ctypes
+
+    from gqa_kernels import _lib
+
+    class FakeLib:
+        def __init__(self, code):
+            self.code = code
+
+        def gqa_device_error(self, code_p, site_p, clear):
+            ctypes.cast(code_p, ctypes.POINTER(ctypes.c_int))[0] = self.code
+            ctypes.cast(site_p, ctypes.POINTER(ctypes.c_int))[0] = 103 if self.code else 0
+            return 0
+
+    dropped = []
+    monkeypatch.setattr(_lib.WORKSPACES, "drop", lambda device: dropped.append(device))
+    monkeypatch.setattr(torch.cuda, "current_device", lambda: 0)
+    monkeypatch.setattr(_lib, "load", lambda: FakeLib(0))
+    assert _lib.device_error() == (0, 0) and dropped == []
+    monkeypatch.setattr(_lib, "load", lambda: FakeLib(5))
+    assert _lib.device_error() == (5, 103)
+    assert dropped == [torch.device("cuda", 0)]

@@ -52,6 +52,8 @@ def test_host_only_entry_points(lib_path):
     for code in range(1, 8):
         assert _lib.strerror(code) and "unknown" not in _lib.strerror(code)
     assert "unknown" in _lib.strerror(99)
+    # the checked build's test hooks are absent from the release library (no GPU touched)
+    assert lib.gqa_debug_inject(0, 0, 1000000) == 2
 
 
 def test_built_for_sm100a(lib_path):

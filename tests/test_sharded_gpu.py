@@ -22,7 +22,8 @@ def _lib_ready(cuda_lib):
 
 
 @pytest.mark.parametrize("shape,world", [((2, 64, 8, 1, 4096, 128), 4), ((1, 32, 8, 3, 1000, 128), 3),
-                                         ((2, 16, 2, 2, 700, 64), 8)])
+                                         ((2, 16, 2, 2, 700, 64), 8),
+                                         ((2, 32, 8, 1, 300, 128), 8)])  # 5 key blocks: 3 ranks empty
 def test_partials_and_combine(shape, world):
     B, Hq, Hkv, Sq, Skv, D = shape
     q, k, v = (t.to(DEVICE) for t in make_inputs(B, Hq, Hkv, Sq, Skv, D, seed=21))

@@ -73,9 +73,15 @@ def _seq_shard_rank(rank, world, B, Hq, Hkv, Sq, Skv, D, causal):
     return float(np.nanmax(np.abs(out - full))), bool(np.array_equal(np.isnan(out), np.isnan(full)))
 
 
-@pytest.mark.parametrize("world,Sq,causal", [(2, 1, True), (2, 5, True), (3, 4, False)])
-def test_seq_sharded_exchange_gloo(world, Sq, causal):
-    res = run_ranks(_seq_shard_rank, world, args=(2, 8, 2, Sq, 300, 32, causal))
+@pytest.mark.parametrize("world,Sq,Skv,causal", [(2, 1, 300, True), (2, 5, 300, True), (3, 4, 300, False),
+                                                 (3, 2, 100, True), (4, 1, 64, True)])
+def test_seq_sharded_exchange_gloo(world, Sq, Skv, causal):
+    """world > ceil(Skv / 64) leaves ranks with no keys: their (-inf, 0, 0) part joins the
+    exchange like any other and weighs 0 in the combine."""
+    if world > -(-Skv // 64):
+        assert any(S.kv_range(Skv, world, r)[0] == S.kv_range(Skv, world, r)[1] for r in range(world))
+    res = run_ranks(_seq_shard_rank, world, args=(2, 8, 2, Sq, Skv, 32, causal))
+    assert len(res) == world
     for rank, (status, val) in res.items():
         assert status == "ok", val
         err, nan_ok = val
