@@ -378,6 +378,186 @@ def make_attention(impl):
     raise SystemExit(f"unknown impl {impl}")
 
 
+# ----------------------------------------------------------------------------- harness parity (benchmark/run.py)
+SWEEP_PREFILL = (2048, 4096, 6144, 8192, 12288, 16384)  # benchmark/run.py:44-46
+SWEEP_DECODE = (2048, 4096, 8192, 16384)
+GATE_LENS = (512, 2048, 4096)
+GATE_TOL = (1e-2, 1e-3)  # the reference harness's gate: inputs N(0,1) * 0.1, max/mean abs
+
+
+@torch.no_grad()
+def fp32_attention(q, k, v):
+    """Bottom-right causal GQA attention in fp32 torch ops on the GPU (TF32 off), per kv
+    head so the scores stay bounded: the reference's oracle math, as a checker."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        B, Hq, Sq, D = q.shape
+        Hkv, Skv = k.shape[1], k.shape[2]
+        G = Hq // Hkv
+        out = torch.empty(q.shape, dtype=torch.float32, device=q.device)
+        mask = (torch.arange(Sq, device=q.device)[:, None] + (Skv - Sq)) < torch.arange(Skv, device=q.device)[None]
+        for b in range(B):
+            for h in range(Hkv):
+                s = q[b, h * G:(h + 1) * G].float() @ k[b, h].float().T * D ** -0.5
+                out[b, h * G:(h + 1) * G] = torch.softmax(s.masked_fill(mask, float("-inf")), -1) @ v[b, h].float()
+        return out
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+def harness_impls():
+    """The harness's kernels: this library, SDPA (K/V expanded over the group outside the
+    timing, is_causal only when seq_q == seq_kv: SDPA's causal mask is top-left aligned,
+    the reference harness's decode trap), and flash_attn when it loads here."""
+    import torch.nn.functional as F
+    from gqa_kernels import gqa_flash_attn
+    impls = {"ours": (lambda q, k, v: (q, k, v), lambda q, k, v: gqa_flash_attn(q, k, v, causal=True))}
+
+    def sdpa_prep(q, k, v):
+        g = q.shape[1] // k.shape[1]
+        return q, k.repeat_interleave(g, 1), v.repeat_interleave(g, 1)
+    impls["sdpa"] = (sdpa_prep, lambda q, k, v: F.scaled_dot_product_attention(q, k, v,
+                                                                               is_causal=q.shape[2] == k.shape[2]))
+    try:
+        from flash_attn import flash_attn_func
+        impls["fa2"] = (lambda q, k, v: tuple(t.transpose(1, 2).contiguous() for t in (q, k, v)),
+                        lambda q, k, v: flash_attn_func(q, k, v, causal=True))
+    except Exception:
+        pass
+    return impls
+
+
+def _to_bhsd(name, o):
+    return o.transpose(1, 2) if name == "fa2" else o
+
+
+def correctness_gate(device, impls, lens=GATE_LENS, log=sys.stderr):
+    """benchmark/run.py:96-137 on this box: every kernel against fp32 attention at the
+    gate lengths, prefill (S x S) and decode (1 x S), B=1, Hq=32, Hkv=8, D=128, bf16
+    inputs N(0,1) * 0.1. Returns (all ok, rows)."""
+    print(f"[correctness] gate: max_abs < {GATE_TOL[0]:g}, mean_abs < {GATE_TOL[1]:g}", file=log)
+    g = torch.Generator(device=device).manual_seed(0)
+    rows, all_ok = [], True
+    for sq, sk, label in [(L, L, "prefill") for L in lens] + [(1, L, "decode") for L in lens]:
+        q = (torch.randn(1, 32, sq, 128, generator=g, device=device) * 0.1).to(torch.bfloat16)
+        k = (torch.randn(1, 8, sk, 128, generator=g, device=device) * 0.1).to(torch.bfloat16)
+        v = (torch.randn(1, 8, sk, 128, generator=g, device=device) * 0.1).to(torch.bfloat16)
+        ref = fp32_attention(q, k, v)
+        for name, (prep, fn) in impls.items():
+            out = _to_bhsd(name, fn(*prep(q, k, v))).float()
+            d = (out - ref).abs()
+            mx, mn = d.max().item(), d.mean().item()
+            ok = mx < GATE_TOL[0] and mn < GATE_TOL[1]
+            all_ok &= ok
+            rows.append({"workload": label, "seq_kv": sk, "impl": name, "max_abs": mx, "mean_abs": mn, "ok": ok})
+            print(f"[correctness] {label:<7} L={sk:>5d}  {name:>4}: max={mx:.2e} mean={mn:.2e}  "
+                  f"{'ok' if ok else 'FAIL'}", file=log)
+    return all_ok, rows
+
+
+def _commit():
+    try:
+        return subprocess.check_output(["git", "rev-parse", "--short=7", "HEAD"], cwd=ROOT,
+                                       stderr=subprocess.DEVNULL).decode().strip()
+    except Exception:
+        return "nogit00"
+
+
+def run_sweep(device, trials=1, quick=False, warmup=25, iters=100, log=sys.stderr):
+    """benchmark/run.py's sweep on this box: the gate, then per length the three kernels
+    timed with CUDA events (warmup, then iters back to back), inputs pre-converted to each
+    kernel's layout outside the timing. Returns the results document in run.py's schema
+    (commit, device, dtype, trials, config, rows) plus rates, roofline fractions, GPU and
+    host-core counts."""
+    impls = harness_impls()
+    ok, gate = correctness_gate(device, impls, log=log)
+    peaks = measured_peaks()
+    prefill, decode = ((8192,), (8192,)) if quick else (SWEEP_PREFILL, SWEEP_DECODE)
+    per_trial = []
+    for _ in range(trials):
+        rows = []
+        for workload, lens in (("prefill", prefill), ("decode", decode)):
+            for L in lens:
+                sq = L if workload == "prefill" else 1
+                g = torch.Generator(device=device).manual_seed(L)
+                q = (torch.randn(1, 32, sq, 128, generator=g, device=device) * 0.1).to(torch.bfloat16)
+                k = (torch.randn(1, 8, L, 128, generator=g, device=device) * 0.1).to(torch.bfloat16)
+                v = (torch.randn(1, 8, L, 128, generator=g, device=device) * 0.1).to(torch.bfloat16)
+                ms = {}
+                for name, (prep, fn) in impls.items():
+                    args = prep(q, k, v)
+                    for _ in range(warmup):
+                        fn(*args)
+                    torch.cuda.synchronize(device)
+                    torch.cuda.reset_peak_memory_stats(device)
+                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a.record()
+                    for _ in range(iters):
+                        fn(*args)
+                    b.record()
+                    torch.cuda.synchronize(device)
+                    ms[name] = (a.elapsed_time(b) / iters, torch.cuda.max_memory_allocated(device) / 2 ** 30)
+                ours = ms["ours"][0]
+                fa2 = ms["fa2"][0] if "fa2" in ms else float("nan")
+                row = {"workload": workload, "seq_kv": L, "ours_ms": ours, "fa2_ms": fa2, "sdpa_ms": ms["sdpa"][0],
+                       "tok_s": sq * 1000.0 / ours, "speedup_vs_fa2": fa2 / ours,
+                       "speedup_vs_sdpa": ms["sdpa"][0] / ours, "peak_mem_gb": ms["ours"][1]}
+                if workload == "prefill":
+                    row["tflops"] = attn_flops(1, 32, sq, L, 128) / (ours * 1e-3) / 1e12
+                    row["roofline_frac"] = row["tflops"] / peaks["bf16"]
+                else:
+                    row["gbs"] = attn_bytes(1, 32, 8, 1, L, 128) / (ours * 1e-3) / 1e9
+                    row["roofline_frac"] = row["gbs"] / peaks["hbm"]
+                rows.append(row)
+                print(f"[{workload}] L={L:>5d}  ours={ours:7.3f}ms  fa2={fa2:7.3f}ms  sdpa={ms['sdpa'][0]:7.3f}ms  "
+                      f"vs_fa2={row['speedup_vs_fa2']:.2f}x  vs_sdpa={row['speedup_vs_sdpa']:.2f}x", file=log)
+        per_trial.append(rows)
+    return sweep_document(aggregate_median(per_trial), ok, gate, trials, torch.cuda.get_device_name(device),
+                          "fa2" in impls, peaks)
+
+
+def aggregate_median(per_trial):
+    """Median over trials of each (workload, seq_kv) row (benchmark/run.py:195-214)."""
+    rows = [dict(r) for r in per_trial[0]]
+    if len(per_trial) > 1:
+        for i, r in enumerate(rows):
+            for key in ("ours_ms", "fa2_ms", "sdpa_ms", "peak_mem_gb"):
+                r[key] = statistics.median(t[i][key] for t in per_trial)
+            sq = r["seq_kv"] if r["workload"] == "prefill" else 1
+            r["tok_s"] = sq * 1000.0 / r["ours_ms"]
+            r["speedup_vs_fa2"], r["speedup_vs_sdpa"] = r["fa2_ms"] / r["ours_ms"], r["sdpa_ms"] / r["ours_ms"]
+            if "tflops" in r:
+                r["tflops"] = attn_flops(1, 32, sq, r["seq_kv"], 128) / (r["ours_ms"] * 1e-3) / 1e12
+            if "gbs" in r:
+                r["gbs"] = attn_bytes(1, 32, 8, 1, r["seq_kv"], 128) / (r["ours_ms"] * 1e-3) / 1e9
+    return rows
+
+
+def sweep_document(rows, gate_ok, gate_rows, trials, device_name, have_fa2, peaks):
+    """The results JSON: benchmark/run.py's schema (commit, device, dtype, trials, config,
+    rows; :265-278) plus the environment, GPU and host-core counts, peaks and the gate."""
+    return {"commit": _commit(), "device": device_name, "dtype": str(torch.bfloat16), "trials": trials,
+            "config": {"batch": 1, "num_heads": 32, "num_kv_heads": 8, "head_dim": 128,
+                       "model": "Llama 3.1 8B attention shape"},
+            "env": {"torch": torch.__version__,
+                    "flash_attn2": "flash_attn.flash_attn_func" if have_fa2 else "unavailable",
+                    "sdpa": "F.scaled_dot_product_attention with pre-expanded K/V"},
+            "n_gpus": 1, "host_cores": host_cores(),
+            "peaks": {"bf16_tflops": peaks["bf16"], "hbm_gbs": peaks["hbm"], "source": peaks["source"]},
+            "gate": {"ok": gate_ok, "tol": list(GATE_TOL), "rows": gate_rows}, "rows": rows}
+
+
+def markdown_table(doc):
+    lines = ["| Workload | seq_kv | ours (ms) | FA2 (ms) | SDPA (ms) | vs FA2 | vs SDPA | roofline | mem (GB) |",
+             "|---|---|---|---|---|---|---|---|---|"]
+    for r in doc["rows"]:
+        lines.append(f"| {r['workload']} | {r['seq_kv']} | {r['ours_ms']:.3f} | {r['fa2_ms']:.3f} | "
+                     f"{r['sdpa_ms']:.3f} | {r['speedup_vs_fa2']:.2f}x | {r['speedup_vs_sdpa']:.2f}x | "
+                     f"{r['roofline_frac']:.3f} | {r['peak_mem_gb']:.2f} |")
+    return "\n".join(lines)
+
+
 # ----------------------------------------------------------------------------- our arm
 def run_attention_workload(wl, world, rank, device, steps, warmup, args):
     from gqa_kernels import sharded as S
@@ -761,7 +941,22 @@ def main():
     ap.add_argument("--decode-steps", type=int, default=5000, help="timed steps of the decode half")
     ap.add_argument("--chunked-steps", type=int, default=200, help="timed steps of the config-4 object")
     ap.add_argument("--long-steps", type=int, default=40, help="timed steps of the config-5 object")
+    ap.add_argument("--sweep", action="store_true",
+                    help="the reference harness on this box (benchmark/run.py): correctness gate of this library, "
+                         "SDPA and flash_attn, then the prefill/decode sweep; prints a table, writes --results")
+    ap.add_argument("--trials", type=int, default=1, help="--sweep: median over this many trials")
+    ap.add_argument("--quick", action="store_true", help="--sweep: the gate and 8K only")
+    ap.add_argument("--results", default=None, help="--sweep: write the results JSON here")
     args = ap.parse_args()
+    if args.sweep:
+        device = torch.device("cuda", 0)
+        torch.cuda.set_device(device)
+        doc = run_sweep(device, trials=args.trials, quick=args.quick)
+        if args.results:
+            with open(args.results, "w") as f:
+                json.dump(doc, f, indent=2)
+        print(markdown_table(doc))
+        sys.exit(0 if doc["gate"]["ok"] else 1)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     wl = WORKLOADS[args.workload]
@@ -782,6 +977,14 @@ def main():
             return
         args.no_e2e = args.no_cpu = True
     world, rank, local = dist_setup(args.gpus)
+    gate = None
+    if comparator and rank == 0:  # the reference harness's gate before any timing (on stderr)
+        dev0 = torch.device("cuda", local)
+        torch.cuda.set_device(dev0)
+        impls = harness_impls()
+        gok, grows = correctness_gate(dev0, {k: impls[k] for k in ("ours", "fa2" if args.impl == "flash_attn"
+                                                                       else "sdpa") if k in impls})
+        gate = {"ok": gok, "tol": list(GATE_TOL), "cases": len(grows)}
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     import gqa_kernels._lib as L
@@ -860,6 +1063,7 @@ def main():
         dist.barrier()
     if comparator:
         line["impl"] = args.impl  # library kernels on the same box: context, not this library
+        line["gate"] = gate
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -218,6 +218,9 @@ __global__ void __launch_bounds__(384, 1)
   pdl_trigger();
   if constexpr (PAGED) {
     if (tid == 0) {
+      // A length above the host's bound is clipped to it (the plan covers seq_kv keys);
+      // the checked build reports such a call.
+      (void)GQA_CHECK(p.seq_lens[b] <= p.seq_kv, 906);
       const int len = max(0, min(p.seq_lens[b], p.seq_kv));
       paged_info[1] = len;
       paged_info[0] = paged_work_tiles<Cfg::kBN>(p, wk, len);
@@ -415,6 +418,30 @@ __global__ void __launch_bounds__(384, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
+      if constexpr (PAGED) {
+        // The tile holding the sequence's end: its keys past the end are masked (P = 0),
+        // but the cache block's stale slots there may hold NaN or Inf, and 0 x NaN would
+        // reach O through the PV MMA. Once V has landed, each thread zeroes its row of V
+        // if that key is past the end (both warpgroups write the same zeros), then fences
+        // the generic writes against the MMA's reads before P is published.
+        const int nv = seq_len() - (j0 + j) * Cfg::kBN;
+        if (nv < Cfg::kBN) {
+          const int tv = 2 * j + 1;
+          ok = mbar_wait(bar_kv_full + 8 * (tv % SLOTS), (tv / SLOTS) & 1, abort_flag, 24 + wg);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+          if (row >= nv) {
+            const uint32_t vrow = kv_smem0 + (tv % SLOTS) * Cfg::kTileBytes + row * 128;
+#pragma unroll
+            for (int c = 0; c < NSUB * 8; ++c)
+              asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(vrow + (c >> 3) * Cfg::kSubBytes +
+                                                                          (c & 7) * 16),
+                           "r"(0u)
+                           : "memory");
+          }
+          fence_proxy_async_smem();
+        }
+      }
       // S row: the second half's TMEM load is in flight while the first half's max
       // is computed (the partial maxima feed the second wait, so they precede it).
       uint32_t sr[128];

@@ -9,6 +9,7 @@
 #include <vector>
 
 #include "gqa_common.cuh"
+#include "gqa_cache.cuh"
 #include "gqa_combine.cuh"
 #include "gqa_prefill.cuh"
 #include "gqa_stream.cuh"
@@ -625,6 +626,56 @@ int gqa_paged_fwd_kv8(const void* q, const void* k_cache, const void* v_cache, v
   return gqa::paged_forward(q, k_cache, v_cache, o, qs, os, block_table, bt_stride, seq_lens, num_seqs, num_heads,
                             num_kv_heads, seq_q, head_dim, block_size, num_blocks, max_seq_len, scale_log2, causal,
                             dtype, workspace, workspace_bytes, stream, true, k_scale, v_scale);
+}
+
+int gqa_paged_kv_append(const void* key, const void* value, const int64_t* k_strides3, const int64_t* v_strides3,
+                        void* k_cache, void* v_cache, const int64_t* slot_mapping, int num_tokens, int num_kv_heads,
+                        int head_dim, int block_size, int num_blocks, int dtype, int cache_fp8, float k_scale,
+                        float v_scale, void* stream) {
+  if (num_tokens < 0 || num_kv_heads <= 0 || block_size <= 0 || num_blocks <= 0) return GQA_ERR_INVALID_ARG;
+  if (head_dim != 64 && head_dim != 128) return GQA_ERR_UNSUPPORTED;
+  if (dtype != GQA_DTYPE_BF16 && dtype != GQA_DTYPE_F16) return GQA_ERR_UNSUPPORTED;
+  if (cache_fp8 && !(k_scale > 0.f && v_scale > 0.f && k_scale < INFINITY && v_scale < INFINITY))
+    return GQA_ERR_INVALID_ARG;
+  if (num_tokens == 0) return GQA_OK;
+  if (!key || !value || !k_strides3 || !v_strides3 || !k_cache || !v_cache || !slot_mapping)
+    return GQA_ERR_INVALID_ARG;
+  if (!aligned16(key) || !aligned16(value) || !aligned16(k_cache) || !aligned16(v_cache)) return GQA_ERR_ALIGNMENT;
+  for (const int64_t* st : {k_strides3, v_strides3}) {
+    if (st[2] != 1) return GQA_ERR_ALIGNMENT;
+    for (int i = 0; i < 2; ++i)
+      if (st[i] < 0 || (st[i] % 8) != 0) return GQA_ERR_ALIGNMENT;
+  }
+  int sm = 0;
+  const int rc = current_device(&sm);
+  if (rc) return rc;
+  AppendParams p{};
+  p.key = reinterpret_cast<const uint16_t*>(key);
+  p.value = reinterpret_cast<const uint16_t*>(value);
+  p.k_st = k_strides3[0]; p.k_sh = k_strides3[1];
+  p.v_st = v_strides3[0]; p.v_sh = v_strides3[1];
+  p.k_cache = k_cache;
+  p.v_cache = v_cache;
+  p.slot_mapping = slot_mapping;
+  p.num_tokens = num_tokens;
+  p.hkv = num_kv_heads;
+  p.num_slots = (int64_t)num_blocks * block_size;
+  p.k_scale = k_scale;
+  p.v_scale = v_scale;
+  const int64_t rows = (int64_t)num_tokens * num_kv_heads;
+  const int blocks = (int)std::min<int64_t>((rows + 7) / 8, (int64_t)sm * 16);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const bool bf = dtype == GQA_DTYPE_BF16, f8 = cache_fp8 != 0;
+#define GQA_APPEND(HD, BF, F8) gqa_kv_append_kernel<HD, BF, F8><<<blocks, 256, 0, st>>>(p)
+  if (head_dim == 128) {
+    if (f8) { if (bf) GQA_APPEND(128, true, true); else GQA_APPEND(128, false, true); }
+    else { if (bf) GQA_APPEND(128, true, false); else GQA_APPEND(128, false, false); }
+  } else {
+    if (f8) { if (bf) GQA_APPEND(64, true, true); else GQA_APPEND(64, false, true); }
+    else { if (bf) GQA_APPEND(64, true, false); else GQA_APPEND(64, false, false); }
+  }
+#undef GQA_APPEND
+  return launch_status();
 }
 
 int gqa_prefill_plan(int batch, int num_heads, int num_kv_heads, int seq_q, int seq_kv, int head_dim, int causal,

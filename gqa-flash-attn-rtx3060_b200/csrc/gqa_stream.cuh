@@ -92,7 +92,7 @@ struct StreamCfg {
   static constexpr int kSmemBytes = kRingBytes + kBarBytes + 64 + 1024;
 };
 
-#define GQA_CBAR() asm volatile("bar.sync 1, 256;" ::: "memory")  // the 8 compute warps
+#define GQA_CBAR() asm volatile("bar.sync 1, %0;" ::"n"(CT) : "memory")  // the compute warps
 
 // FP8: K and V are e4m3 (HD = 128, so a key row is 128 bytes, the shared-memory
 // geometry of a 16-bit HD = 64 row); Q and O keep the 16-bit I/O type. Both MMAs
@@ -186,6 +186,9 @@ __global__ void __launch_bounds__(288, 1)
   // Highest key (local, exclusive) any valid row of this unit may see.
   int kv_end = p.seq_kv;
   if (paged) {
+    // A length above the host's bound is clipped to it (the plan covers seq_kv keys);
+    // the checked build reports such a call.
+    (void)GQA_CHECK(p.seq_lens[b] <= p.seq_kv, 906);
     kv_end = max(0, min(kv_end, p.seq_lens[b]));
     off = kv_end - p.seq_q;  // the sequence's queries are its last seq_q positions
   }
@@ -353,6 +356,20 @@ __global__ void __launch_bounds__(288, 1)
     const uint32_t kst = base + slot * Cfg::kStageBytes;
     const uint32_t vst = kst + Cfg::kTileBytes;
     const int key_w = k_begin + t * Cfg::kBN + ks * NKW;  // first key of this warp's block
+    if (key_w < k_end && key_w + NKW > k_end) {
+      // The block holding the chunk's end: keys past it are masked (P = 0), but a paged
+      // sequence's last cache block holds stale slots there and 0 x NaN would still
+      // reach O through the MMA, so this warp zeroes the V rows of those keys (only it
+      // reads them). The stage is the chunk's last: no copy refills the slot afterwards.
+      const int first = k_end - key_w;
+      constexpr int kRowChunks = Cfg::kNSub * 8;  // 16-byte chunks of one V row
+      for (int i = lane; i < (NKW - first) * kRowChunks; i += 32) {
+        const int r = ks * NKW + first + i / kRowChunks, c = i % kRowChunks;
+        const uint32_t addr = vst + (c >> 3) * Cfg::kSubBytes + r * 128 + (c & 7) * 16;
+        asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(0u) : "memory");
+      }
+      __syncwarp();
+    }
     if constexpr (NT) {
       if (key_w < k_end) {
         // ---- S^T = K Q^T: 16 keys (M) x 8 rows (N). Two partial sums (even and odd

@@ -56,6 +56,7 @@ SIGNATURES = {
     "gqa_prefill_plan": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, ctypes.POINTER(ctypes.c_int)]),
     "gqa_paged_fwd_kv8": (_I, [_P, _P, _P, _P, _I64P, _I64P, _P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _F,
                                _F, _I, _I, _P, _SZ, _P]),
+    "gqa_paged_kv_append": (_I, [_P, _P, _I64P, _I64P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _F, _P]),
     "gqa_debug_inject": (_I, [_I, _I, ctypes.c_longlong]),
     "gqa_debug_exp2_poly2": (_I, [_P, _P, _I, _P]),
 }

@@ -197,8 +197,9 @@ int gqa_paged_decode(const void* q, const void* k_cache, const void* v_cache, vo
  * path's rule); without, all seq_lens[b] keys. Rows that see no key give NaN.
  * Short chunks (group * seq_q <= 64) run the streaming kernel, longer ones the
  * tcgen05 prefill kernel, whose producer reads K/V tiles through the block
- * table. Cache slots past seq_lens[b] in a sequence's last block are read and
- * masked, so they must hold finite values (a zero-initialised cache does).
+ * table. Cache slots past seq_lens[b] in a sequence's last block are read but
+ * never reach O (their V rows are zeroed in shared memory before the PV MMA), so
+ * stale or non-finite values there are harmless.
  * The key split is sized by max_seq_len; its workspace (zeroed before first
  * use; every call leaves it zero) is gqa_paged_fwd_workspace_bytes(). Called
  * with seq_q = 1 and causal = 0 this is gqa_paged_decode.
@@ -230,6 +231,26 @@ int gqa_paged_fwd_kv8(const void* q, const void* k_cache, const void* v_cache, v
                       int num_seqs, int num_heads, int num_kv_heads, int seq_q, int head_dim, int block_size,
                       int num_blocks, int max_seq_len, float scale_log2, float k_scale, float v_scale, int causal,
                       int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Cache write of the paged interface (vLLM's reshape_and_cache_flash): token t's K
+ * and V rows, key/value (num_tokens, num_kv_heads, head_dim) with element strides
+ * k_strides3 / v_strides3 (d stride 1, the others multiples of 8 elements), go to
+ * slot slot_mapping[t] (int64; block = slot / block_size, position = slot %
+ * block_size) of the (num_blocks, block_size, num_kv_heads, head_dim) caches. A
+ * negative slot is a padding token and is skipped. 16-bit caches (dtype) receive the
+ * rows unchanged; with cache_fp8 the caches are e4m3 and receive x / k_scale (x /
+ * v_scale) rounded to nearest even and saturated to +-448, vLLM's convention (real
+ * value = stored value x scale; scales > 0). A slot >= num_blocks * block_size is not
+ * written: its row is skipped and GQA_ERR_INVALID_ARG is recorded in the device error
+ * word (site 201; gqa_device_error). Tokens must map to distinct slots.
+ * No reference counterpart: the cache-write half of the roadmap's vLLM-shaped
+ * interface (README.md:144).
+ */
+int gqa_paged_kv_append(const void* key, const void* value, const int64_t* k_strides3, const int64_t* v_strides3,
+                        void* k_cache, void* v_cache, const int64_t* slot_mapping, int num_tokens, int num_kv_heads,
+                        int head_dim, int block_size, int num_blocks, int dtype, int cache_fp8, float k_scale,
+                        float v_scale, void* stream);
 
 /*
  * The tcgen05 prefill path's launch plan for a shape on `sm_count` SMs, without

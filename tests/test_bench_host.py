@@ -126,3 +126,48 @@ def test_sharded_parity_check_over_gloo():
     for rank, (status, res) in out.items():
         assert status == "ok", res
         assert res == (True, False), (rank, res)
+
+
+def _row(workload, L, ours, fa2, sdpa):
+    sq = L if workload == "prefill" else 1
+    return {"workload": workload, "seq_kv": L, "ours_ms": ours, "fa2_ms": fa2, "sdpa_ms": sdpa,
+            "tok_s": sq * 1000.0 / ours, "speedup_vs_fa2": fa2 / ours, "speedup_vs_sdpa": sdpa / ours,
+            "peak_mem_gb": 0.1, "roofline_frac": 0.5}
+
+
+def test_sweep_results_keep_the_reference_harness_schema(bench):
+    """--sweep writes benchmark/run.py's results schema (commit, device, dtype, trials,
+    config, rows with the same row keys) plus its own keys."""
+    trials = [[_row("prefill", 2048, 0.03, 0.09, 0.04), _row("decode", 2048, 0.008, 0.02, 0.009)],
+              [_row("prefill", 2048, 0.05, 0.08, 0.05), _row("decode", 2048, 0.006, 0.02, 0.01)],
+              [_row("prefill", 2048, 0.04, 0.10, 0.06), _row("decode", 2048, 0.007, 0.03, 0.008)]]
+    rows = bench.aggregate_median(trials)
+    assert rows[0]["ours_ms"] == 0.04 and rows[1]["sdpa_ms"] == 0.009
+    assert rows[0]["speedup_vs_fa2"] == pytest.approx(0.09 / 0.04)
+    doc = bench.sweep_document(rows, True, [], 3, "NVIDIA B200", True, bench.measured_peaks())
+    for key in ("commit", "device", "dtype", "trials", "config", "rows"):
+        assert key in doc
+    assert doc["config"] == {"batch": 1, "num_heads": 32, "num_kv_heads": 8, "head_dim": 128,
+                             "model": "Llama 3.1 8B attention shape"}
+    ref_row_keys = {"workload", "seq_kv", "ours_ms", "fa2_ms", "sdpa_ms", "tok_s", "speedup_vs_fa2",
+                    "speedup_vs_sdpa", "peak_mem_gb"}
+    assert all(ref_row_keys <= set(r) for r in doc["rows"])
+    import json
+    json.dumps(doc)  # serialisable
+    table = bench.markdown_table(doc)
+    assert table.count("\n") == 1 + len(rows) and "| prefill | 2048 |" in table
+
+
+def test_sweep_lengths_are_the_reference_harness_lengths(bench):
+    assert bench.SWEEP_PREFILL == (2048, 4096, 6144, 8192, 12288, 16384)
+    assert bench.SWEEP_DECODE == (2048, 4096, 8192, 16384)
+    assert bench.GATE_LENS == (512, 2048, 4096) and bench.GATE_TOL == (1e-2, 1e-3)
+
+
+def test_fp32_attention_checker_matches_the_oracle(bench):
+    """The harness gate's fp32 checker against the torch restatement of the reference oracle."""
+    import torch
+    from oracle import gqa_oracle_torch as T
+    q, k, v = _rows_setup(seed=3, Sq=20, Skv=50)
+    ref = T.gqa_reference_blocked(q, k, v, causal=True)
+    assert torch.allclose(bench.fp32_attention(q, k, v), ref, atol=1e-6, rtol=1e-5)

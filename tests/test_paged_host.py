@@ -109,3 +109,34 @@ def test_paged_oracle_equals_the_dense_oracle_on_gathered_keys():
         ref = O.gqa_reference(q[i:i + 1], k, v, causal=True)[0]
         np.testing.assert_allclose(out[i], ref, rtol=1e-6, atol=1e-6, equal_nan=True)
     assert np.isnan(out[0, :, :2]).all() and not np.isnan(out[0, :, 2:]).any()  # 3 keys, 5 queries
+
+
+def test_kv_append_argument_checks_before_the_device():
+    """paged_kv_append validates shapes and dtypes on CPU tensors before any launch."""
+    from gqa_kernels.paged import paged_kv_append
+    k = torch.zeros(4, 2, 128, dtype=torch.bfloat16)
+    kc = torch.zeros(3, 64, 2, 128, dtype=torch.bfloat16)
+    slots = torch.zeros(4, dtype=torch.int64)
+    with pytest.raises(ValueError):
+        paged_kv_append(k, k[:, :1], kc, kc, slots)  # value shape
+    with pytest.raises(ValueError):
+        paged_kv_append(k, k, kc[:, :, :1], kc[:, :, :1], slots)  # cache heads
+    with pytest.raises(TypeError):
+        paged_kv_append(k, k, kc.half(), kc.half(), slots)  # cache dtype
+    with pytest.raises(TypeError):
+        paged_kv_append(k, k, kc, kc, slots.int())  # slot dtype
+    with pytest.raises(ValueError):
+        paged_kv_append(k, k, kc.to(torch.float8_e4m3fn), kc.to(torch.float8_e4m3fn), slots, k_scale=0.0)
+    with pytest.raises(ValueError):
+        paged_kv_append(k, k, kc, kc, slots)  # CPU tensors: not CUDA memory
+
+
+def test_paged_attention_layer_arguments():
+    from gqa_kernels.paged import PagedAttention
+    with pytest.raises(ValueError):
+        PagedAttention(32, 128, num_kv_heads=6)
+    with pytest.raises(ValueError):
+        PagedAttention(32, 128, kv_cache_dtype="fp8_e5m2")
+    layer = PagedAttention(32, 128, num_kv_heads=8, kv_cache_dtype="fp8_e4m3")
+    cache = layer.allocate_kv_cache(4, 64, torch.bfloat16, "cpu")
+    assert cache.shape == (2, 4, 64, 8, 128) and cache.dtype == torch.float8_e4m3fn

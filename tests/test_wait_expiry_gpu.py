@@ -28,7 +28,7 @@ LOG2E = 1.4426950408889634
 GQA_ERR_TIMEOUT = 5
 LIMIT_NS = 20_000_000
 
-PREFILL_SITES = set(range(1, 24))     # producer 1-2, MMA issuer 10-19, softmax 20-23
+PREFILL_SITES = set(range(1, 26))     # producer 1-2, MMA issuer 10-19, softmax 20-25
 STREAM_SITES = set(range(101, 105))   # producer 101-102, compute 103, combine 104
 
 
