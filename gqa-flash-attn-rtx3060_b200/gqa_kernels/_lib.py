@@ -104,9 +104,21 @@ def check_one_device(*tensors):
             raise ValueError("tensors must be on one device")
 
 
+_STRIDES = {}
+
+
 def strides(t, n=4):
-    """Element strides of `t` as a ctypes int64 array."""
-    return (ctypes.c_int64 * n)(*t.stride())
+    """Element strides of `t` as a ctypes int64 array (one array per distinct stride
+    tuple, reused: the library only reads it during the call)."""
+    st = t.stride()
+    if len(st) != n:
+        raise ValueError(f"expected a {n}-d tensor")
+    arr = _STRIDES.get(st)
+    if arr is None:
+        if len(_STRIDES) > 4096:
+            _STRIDES.clear()
+        arr = _STRIDES[st] = (ctypes.c_int64 * n)(*st)
+    return arr
 
 
 def dtype_code(t):
@@ -118,7 +130,42 @@ def dtype_code(t):
 
 
 def stream_ptr(device):
-    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+    """The raw cudaStream_t of the current stream of `device`, as an int."""
+    return torch._C._cuda_getCurrentRawStream(device.index)
+
+
+class _NoGuard:
+    def __enter__(self):
+        return None
+
+    def __exit__(self, *exc):
+        return False
+
+
+_NO_GUARD = _NoGuard()
+
+
+def on_device(device):
+    """Context making `device` current for a launch: a no-op when it already is (the
+    usual case), torch.cuda.device(device) otherwise."""
+    if device.index == torch.cuda.current_device():
+        return _NO_GUARD
+    return torch.cuda.device(device)
+
+
+_WS_BYTES = {}
+
+
+def workspace_bytes(query, *shape):
+    """lib.<query>(*shape) on the current device, remembered per (device, query, shape):
+    the answer depends on nothing else (the device's SM count sizes the split)."""
+    key = (torch.cuda.current_device(), query, shape)
+    n = _WS_BYTES.get(key)
+    if n is None:
+        if len(_WS_BYTES) > 4096:
+            _WS_BYTES.clear()
+        n = _WS_BYTES[key] = getattr(load(), query)(*shape)
+    return n
 
 
 def tma_compatible(t):
@@ -147,8 +194,7 @@ class WorkspaceCache:
         self._lock = threading.Lock()
 
     def get(self, device, nbytes, signature):
-        stream = torch.cuda.current_stream(device)
-        key = (device.index, stream.cuda_stream)
+        key = (device.index, stream_ptr(device))
         with self._lock:
             ent = self._bufs.get(key)
             if ent is None or ent[0].numel() < nbytes:

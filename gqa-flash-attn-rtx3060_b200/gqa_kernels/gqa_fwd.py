@@ -13,8 +13,6 @@ the HBM-streaming kernel for fewer (decode-shaped calls).
 """
 import ctypes
 
-import torch
-
 from . import _lib
 
 
@@ -32,7 +30,8 @@ def launch_fwd(q, k, v, o, causal, scale_log2):
     _, num_kv_heads, seq_kv, _ = k.shape
     lib = _lib.load()
     dev = q.device
-    ws_bytes = lib.gqa_fwd_workspace_bytes(batch, num_heads, num_kv_heads, seq_q, seq_kv, head_dim)
+    ws_bytes = _lib.workspace_bytes("gqa_fwd_workspace_bytes", batch, num_heads, num_kv_heads, seq_q, seq_kv,
+                                     head_dim)
     ws_ptr = None
     if ws_bytes:
         ws = _lib.WORKSPACES.get(dev, ws_bytes, ("fwd", batch, num_heads, num_kv_heads, seq_q, seq_kv, head_dim))
@@ -65,7 +64,7 @@ class _FwdLauncher:
             raise ValueError("seq_q / seq_kv must match the tensors")
         if Q.shape[1] != GROUP_SIZE * K.shape[1] or Q.shape[3] != HEAD_DIM:
             raise ValueError("GROUP_SIZE / HEAD_DIM must match the tensors")
-        with torch.cuda.device(Q.device):
+        with _lib.on_device(Q.device):
             launch_fwd(Q, K, V, O, bool(IS_CAUSAL), float(scale))
 
 

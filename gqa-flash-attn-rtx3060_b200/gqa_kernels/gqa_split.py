@@ -29,8 +29,9 @@ def split_kv_forward(q, k, v, causal, splits):
     scale_log2 = (head_dim ** -0.5) * LOG2E
     o = torch.empty_like(q)
     lib = _lib.load()
-    with torch.cuda.device(q.device):
-        ws_bytes = lib.gqa_split_fused_workspace_bytes(batch, num_heads, num_kv_heads, seq_q, seq_kv, head_dim)
+    with _lib.on_device(q.device):
+        ws_bytes = _lib.workspace_bytes("gqa_split_fused_workspace_bytes", batch, num_heads, num_kv_heads, seq_q,
+                                         seq_kv, head_dim)
         ws = _lib.WORKSPACES.get(q.device, ws_bytes,
                                  ("split", batch, num_heads, num_kv_heads, seq_q, seq_kv, head_dim))
         rc = lib.gqa_split_fused(
@@ -76,7 +77,7 @@ class _SplitFirstLauncher:
         for t in (Mp, Lp, Ap):
             if t.dtype != torch.float32:
                 raise TypeError("partials must be float32")
-        with torch.cuda.device(Q.device):
+        with _lib.on_device(Q.device):
             rc = _lib.load().gqa_split_first(
                 ctypes.c_void_p(Q.data_ptr()), ctypes.c_void_p(K.data_ptr()), ctypes.c_void_p(V.data_ptr()),
                 ctypes.c_void_p(Mp.data_ptr()), ctypes.c_void_p(Lp.data_ptr()), ctypes.c_void_p(Ap.data_ptr()),
@@ -102,7 +103,7 @@ class _SplitReduceLauncher:
         batch, num_heads, seq_q, head_dim = O.shape
         if head_dim != HEAD_DIM:
             raise ValueError("HEAD_DIM must match O")
-        with torch.cuda.device(O.device):
+        with _lib.on_device(O.device):
             rc = _lib.load().gqa_split_reduce(
                 ctypes.c_void_p(Mp.data_ptr()), ctypes.c_void_p(Lp.data_ptr()), ctypes.c_void_p(Ap.data_ptr()),
                 ctypes.c_void_p(O.data_ptr()), _lib.strides(Mp), _lib.strides(Ap, 5), _lib.strides(O),

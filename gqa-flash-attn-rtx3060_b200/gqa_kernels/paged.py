@@ -31,8 +31,8 @@ keys (and its queries are aligned to that length), so pass a true bound or leave
 the default, the block table's capacity; the checked build (build.py --debug)
 reports such a call as GQA_ERR_DEBUG_CHECK in the device error word.
 """
-from dataclasses import dataclass
 import ctypes
+from dataclasses import dataclass
 
 import torch
 
@@ -77,8 +77,9 @@ def paged_decode(query, key_cache, value_cache, block_tables, seq_lens, max_seq_
     scale = head_dim ** -0.5 if scale is None else float(scale)
     out = torch.empty_like(query)
     lib = _lib.load()
-    with torch.cuda.device(query.device):
-        ws_bytes = lib.gqa_paged_decode_workspace_bytes(num_seqs, num_heads, num_kv_heads, max_seq_len, head_dim)
+    with _lib.on_device(query.device):
+        ws_bytes = _lib.workspace_bytes("gqa_paged_decode_workspace_bytes", num_seqs, num_heads, num_kv_heads,
+                                         max_seq_len, head_dim)
         ws = _lib.WORKSPACES.get(query.device, ws_bytes,
                                  ("paged", num_seqs, num_heads, num_kv_heads, max_seq_len, head_dim))
         rc = lib.gqa_paged_decode(
@@ -162,9 +163,9 @@ def paged_prefill(query, key_cache, value_cache, block_tables, seq_lens, max_seq
     else:
         _lib.check_one_device(query, out)
     lib = _lib.load()
-    with torch.cuda.device(query.device):
-        ws_bytes = lib.gqa_paged_fwd_workspace_bytes(num_seqs, num_heads, num_kv_heads, chunk_len, max_seq_len,
-                                                     head_dim)
+    with _lib.on_device(query.device):
+        ws_bytes = _lib.workspace_bytes("gqa_paged_fwd_workspace_bytes", num_seqs, num_heads, num_kv_heads, chunk_len,
+                                         max_seq_len, head_dim)
         ws = _lib.WORKSPACES.get(query.device, ws_bytes,
                                  ("paged_fwd", num_seqs, num_heads, num_kv_heads, chunk_len, max_seq_len, head_dim))
         fp8 = key_cache.dtype == torch.float8_e4m3fn
@@ -222,7 +223,7 @@ def paged_kv_append(key, value, key_cache, value_cache, slot_mapping, k_scale=1.
     value = value if _lib.tma_compatible(value) else value.contiguous()
     slot_mapping = slot_mapping.contiguous()
     lib = _lib.load()
-    with torch.cuda.device(key.device):
+    with _lib.on_device(key.device):
         rc = lib.gqa_paged_kv_append(
             ctypes.c_void_p(key.data_ptr()), ctypes.c_void_p(value.data_ptr()), _lib.strides(key, 3),
             _lib.strides(value, 3), ctypes.c_void_p(key_cache.data_ptr()), ctypes.c_void_p(value_cache.data_ptr()),

@@ -86,8 +86,9 @@ def partial_forward(q, k_shard, v_shard, causal, kv_offset, seq_kv_total, out=No
         out = torch.empty(total, dtype=torch.float32, device=q.device)
     m, l, acc = out[:rows], out[rows:2 * rows], out[acc_off:]
     lib = _lib.load()
-    with torch.cuda.device(q.device):
-        ws_bytes = lib.gqa_partial_workspace_bytes(batch, num_heads, num_kv_heads, seq_q, n_local, head_dim)
+    with _lib.on_device(q.device):
+        ws_bytes = _lib.workspace_bytes("gqa_partial_workspace_bytes", batch, num_heads, num_kv_heads, seq_q,
+                                         n_local, head_dim)
         ws = _lib.WORKSPACES.get(q.device, ws_bytes,
                                  ("partial", batch, num_heads, num_kv_heads, seq_q, n_local, head_dim))
         rc = lib.gqa_partial(
@@ -139,7 +140,7 @@ def combine_partials(gathered, q_shape, dtype, device, out=None):
     nparts, stride = gathered.shape
     if out is None:
         out = torch.empty(q_shape, dtype=dtype, device=device)
-    with torch.cuda.device(device):
+    with _lib.on_device(device):
         rc = _lib.load().gqa_lse_combine(
             ctypes.c_void_p(gathered.data_ptr()), ctypes.c_void_p(gathered.data_ptr() + 4 * rows),
             ctypes.c_void_p(gathered.data_ptr() + 4 * acc_off), nparts, stride, stride,

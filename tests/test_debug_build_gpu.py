@@ -63,3 +63,30 @@ def test_debug_build_checks_pass_and_match(libs, shape):
     b = _fwd(dbg, q, k, v)
     assert _error(dbg) == (0, 0)
     assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+
+
+def test_debug_build_reports_a_length_above_max_seq_len(libs):
+    """A paged call whose seq_lens[b] exceeds the host's max_seq_len is clipped to the bound
+    (the plan covers max_seq_len keys); the checked build reports it as GQA_ERR_DEBUG_CHECK
+    (site 906), on the streaming path (decode) and on the tcgen05 path (long chunks)."""
+    rel, dbg = libs
+    Hq, Hkv, D, bs = 32, 8, 128, 64
+    g = torch.Generator(device="cuda").manual_seed(3)
+    kc = torch.randn(8, bs, Hkv, D, generator=g, device="cuda").to(torch.bfloat16)
+    vc = torch.randn_like(kc)
+    bt = torch.arange(8, dtype=torch.int32, device="cuda").view(1, 8)
+    sl = torch.tensor([500], dtype=torch.int32, device="cuda")
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for chunk in (1, 128):
+        q = torch.randn(1, Hq, chunk, D, generator=g, device="cuda").to(torch.bfloat16)
+        o = torch.empty_like(q)
+        ws = torch.zeros(1 << 22, dtype=torch.uint8, device="cuda")
+        for lib, max_len, want in ((dbg, 512, (0, 0)), (dbg, 256, (9, 906)), (rel, 256, (0, 0))):
+            rc = lib.gqa_paged_fwd(ctypes.c_void_p(q.data_ptr()), ctypes.c_void_p(kc.data_ptr()),
+                                   ctypes.c_void_p(vc.data_ptr()), ctypes.c_void_p(o.data_ptr()), _lib.strides(q),
+                                   _lib.strides(o), ctypes.c_void_p(bt.data_ptr()), 8, ctypes.c_void_p(sl.data_ptr()),
+                                   1, Hq, Hkv, chunk, D, bs, 8, max_len, ctypes.c_float(D ** -0.5 * LOG2E), 1, 1,
+                                   ctypes.c_void_p(ws.data_ptr()), ctypes.c_size_t(ws.numel()), stream)
+            assert rc == 0, rc
+            torch.cuda.synchronize()
+            assert _error(lib) == want, (chunk, max_len)
