@@ -125,8 +125,11 @@ struct PrefillCfg {
   static constexpr int kQOff = 0;
   static constexpr int kKVOff = 2 * kTileBytes;
   static constexpr int kBarOff = kKVOff + kSlots * kTileBytes;
-  // barriers: q_full[2] kv_full[S] kv_empty[S] s_full[2] p_full[2 tiles][2 halves] o_final[2] mma_done
-  static constexpr int kNumBars = 2 + 2 * kSlots + 2 + 4 + 2 + 1;
+  // P is published to the MMA warp in kPParts column parts per tile, each with its own
+  // barrier, so the PV UMMAs of a part start while the next part is computed.
+  static constexpr int kPParts = 2;
+  // barriers: q_full[2] kv_full[S] kv_empty[S] s_full[2] p_full[2 tiles][kPParts] o_final[2] mma_done
+  static constexpr int kNumBars = 2 + 2 * kSlots + 2 + 2 * kPParts + 2 + 1;
   // tmem base, abort flag, last-CTA flag, paged key tiles, paged sequence length
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kSmemBytes = kMiscOff + 32 + 1024;  // + alignment slack
@@ -167,8 +170,8 @@ __global__ void __launch_bounds__(384, 1)
   const uint32_t bar_kv_full = bars + 16;                // [SLOTS]
   const uint32_t bar_kv_empty = bar_kv_full + 8 * SLOTS; // [SLOTS]
   const uint32_t bar_s_full = bar_kv_empty + 8 * SLOTS;  // [2]
-  const uint32_t bar_p_full = bar_s_full + 16;           // [2][2]: (tile, 64-key half of P)
-  const uint32_t bar_o_final = bar_p_full + 32;          // [2]
+  const uint32_t bar_p_full = bar_s_full + 16;           // [2][kPParts]: (tile, column part of P)
+  const uint32_t bar_o_final = bar_p_full + 16 * Cfg::kPParts;  // [2]
   const uint32_t bar_mma_done = bar_o_final + 16;
   uint32_t* tmem_base_ptr = reinterpret_cast<uint32_t*>(smem + Cfg::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kMiscOff + 4);
@@ -203,8 +206,7 @@ __global__ void __launch_bounds__(384, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar_s_full + 8 * i, 1);
-      mbar_init(bar_p_full + 16 * i, 128);
-      mbar_init(bar_p_full + 16 * i + 8, 128);
+      for (int h = 0; h < Cfg::kPParts; ++h) mbar_init(bar_p_full + 8 * (Cfg::kPParts * i + h), 128);
       mbar_init(bar_o_final + 8 * i, 1);
     }
     mbar_init(bar_mma_done, 1);
@@ -317,14 +319,15 @@ __global__ void __launch_bounds__(384, 1)
           umma_ss(tS, desc_sw128_kmajor(qa + o), desc_sw128_kmajor(kb + o), idesc_qk, k > 0 ? 1u : 0u);
         }
       };
-      // O_i += P_i V over the 64-key half h of the tile (4 UMMAs of 16 keys each).
+      // O_i += P_i V over column part h of the tile (UMMAs of 16 keys each).
       auto issue_pv = [&](int i, int slot, int h, bool acc) {
         const uint32_t tS = tmem_base + (i ? Cfg::kColS1 : Cfg::kColS0);
         const uint32_t tO = tmem_base + (i ? Cfg::kColO1 : Cfg::kColO0);
         const uint32_t vb = kv_smem0 + slot * Cfg::kTileBytes;
+        constexpr int kPerPart = Cfg::kBN / 16 / Cfg::kPParts;
 #pragma unroll
-        for (int kk = 0; kk < Cfg::kBN / 32; ++kk) {
-          const int k = h * (Cfg::kBN / 32) + kk;
+        for (int kk = 0; kk < kPerPart; ++kk) {
+          const int k = h * kPerPart + kk;
           // P: 16 keys = 8 TMEM columns of packed 16-bit pairs; V: 16 key rows of 128 B.
           umma_ts(tO, tS + k * 8, desc_sw128_mnmajor(vb + k * 16 * 128, Cfg::kSubBytes), idesc_pv,
                   (acc || k > 0) ? 1u : 0u);
@@ -343,12 +346,16 @@ __global__ void __launch_bounds__(384, 1)
           const int tv = 2 * j + 1, sv = tv % SLOTS;
           const int tk = 2 * j + 2, sk = tk % SLOTS;
           if (!mbar_wait(bar_kv_full + 8 * sv, (tv / SLOTS) & 1, abort_flag, 13)) break;
-          if (!mbar_wait(bar_p_full, j & 1, abort_flag, 14)) break;
-          tc_fence_after();
-          issue_pv(0, sv, 0, j > 0);
-          if (!mbar_wait(bar_p_full + 8, j & 1, abort_flag, 18)) break;
-          tc_fence_after();
-          issue_pv(0, sv, 1, true);
+          bool pv_ok = true;
+#pragma unroll
+          for (int h = 0; h < Cfg::kPParts && pv_ok; ++h) {
+            pv_ok = mbar_wait(bar_p_full + 8 * h, j & 1, abort_flag, h ? 18 : 14);
+            if (pv_ok) {
+              tc_fence_after();
+              issue_pv(0, sv, h, h > 0 || j > 0);
+            }
+          }
+          if (!pv_ok) break;
           const bool more = (j + 1 < nk);
           if (more) {
             if (!mbar_wait(bar_kv_full + 8 * sk, (tk / SLOTS) & 1, abort_flag, 15)) break;
@@ -358,12 +365,15 @@ __global__ void __launch_bounds__(384, 1)
           } else {
             umma_commit(bar_o_final);
           }
-          if (!mbar_wait(bar_p_full + 16, j & 1, abort_flag, 16)) break;
-          tc_fence_after();
-          issue_pv(1, sv, 0, j > 0);
-          if (!mbar_wait(bar_p_full + 24, j & 1, abort_flag, 19)) break;
-          tc_fence_after();
-          issue_pv(1, sv, 1, true);
+#pragma unroll
+          for (int h = 0; h < Cfg::kPParts && pv_ok; ++h) {
+            pv_ok = mbar_wait(bar_p_full + 8 * (Cfg::kPParts + h), j & 1, abort_flag, h ? 19 : 16);
+            if (pv_ok) {
+              tc_fence_after();
+              issue_pv(1, sv, h, h > 0 || j > 0);
+            }
+          }
+          if (!pv_ok) break;
           umma_commit(bar_kv_empty + 8 * sv);  // V_j consumed
           if (more) {
             issue_qk(1, sk);
@@ -391,7 +401,7 @@ __global__ void __launch_bounds__(384, 1)
     const uint32_t tS = tmem_base + lane_off + (wg ? Cfg::kColS1 : Cfg::kColS0);
     const uint32_t tO = tmem_base + lane_off + (wg ? Cfg::kColO1 : Cfg::kColO0);
     const uint32_t s_full = bar_s_full + 8 * wg;
-    const uint32_t p_full = bar_p_full + 16 * wg;  // + 8 for the second half
+    const uint32_t p_full = bar_p_full + 8 * Cfg::kPParts * wg;  // + 8 per column part
 
     const int g = row / p.bm;
     const int pos = p0 + wg * p.bm + (row - g * p.bm);
@@ -503,19 +513,20 @@ __global__ void __launch_bounds__(384, 1)
         l_run *= fast_exp2(m_run - m_new);
         m_run = m_new;
       }
-      // P = exp2(S * scale - m), written over S as packed 16-bit pairs, in two 64-key
-      // halves so the PV MMAs of the first half start while the second is computed.
+      // P = exp2(S * scale - m), written over S as packed 16-bit pairs, in kPParts column
+      // parts so the PV MMAs of a part start while the next one is computed.
       // One column pair in eight takes the polynomial exp2 on the FMA pipe, the rest
       // the MUFU ex2; the row sum and the scale use packed two-lane fp32 math.
       const float2 sc2 = make_float2(scale, scale);
       const float2 nm2 = make_float2(-m_run, -m_run);
       float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      constexpr int kPairs = 64 / Cfg::kPParts;  // column pairs (packed TMEM columns) per part
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t pk[32];
+      for (int h = 0; h < Cfg::kPParts; ++h) {
+        uint32_t pk[kPairs];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const int col = 64 * h + 2 * c;
+        for (int c = 0; c < kPairs; ++c) {
+          const int col = 2 * kPairs * h + 2 * c;
           const float2 x = fma2(make_float2(__uint_as_float(sr[col]), __uint_as_float(sr[col + 1])), sc2, nm2);
           float2 pv;
           if ((c & 7) >= Cfg::kMufuPairsPer8) {
@@ -527,7 +538,7 @@ __global__ void __launch_bounds__(384, 1)
           sum2[c & 3] = add2(sum2[c & 3], pv);
           pk[c] = pack2<BF16>(pv.x, pv.y);
         }
-        tmem_st32(tS + 32 * h, pk);
+        if constexpr (kPairs == 32) tmem_st32(tS + 32 * h, pk); else tmem_st16(tS + 16 * h, pk);
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(p_full + 8 * h);
