@@ -1073,18 +1073,21 @@ def main():
 
 def main_reference(args, wl, steps):
     """The reference arm: the reference's CPU path, its torch attention
-    (tests/reference.py, restated in oracle/gqa_oracle_torch.py) in fp32 on every host core."""
+    (tests/reference.py, restated in oracle/gqa_oracle_torch.py) in fp32 on every host core.
+    A step is a bounded sample of the workload: enough row blocks of one (batch, kv head)
+    unit for about a quarter second of CPU work. The warm-up steps run untimed (the thread
+    pool spins up there); the timed steps are capped at about two minutes in total."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    # each step is one block of query rows; run as many of the requested warmup + steps
-    # as fit in about two minutes (at least 3)
-    _, _, _, per, _ = cpu_sample(wl, budget_s=0.0, steps=1, kind="torch")
-    total = steps + args.warmup
-    n_run = max(3, min(total, int(120.0 / max(per[0], 1e-3))))
-    val, unit, sample, per, cores = cpu_sample(wl, budget_s=0.0, steps=n_run, kind="torch")
-    ms_step = statistics.mean(per) * 1e3
+    _, _, _, per, _ = cpu_sample(wl, budget_s=0.0, steps=3, kind="torch")  # thread pool up, block cost
+    blocks = max(1, int(0.25 / max(min(per), 1e-4)))
+    warm = min(args.warmup, max(1, int(10.0 / (blocks * min(per)))))
+    cpu_sample(wl, budget_s=0.0, steps=warm * blocks, kind="torch")
+    n_timed = max(3, min(steps, int(120.0 / (blocks * min(per)))))
+    val, unit, sample, per, cores = cpu_sample(wl, budget_s=0.0, steps=n_timed * blocks, kind="torch")
+    ms_step = sum(per) / n_timed * 1e3
     line = {
         "metric": METRIC if args.workload in ("prefill", "decode") else f"{args.workload} {unit}",
         "value": round(val, 6), "unit": unit, "impl": "reference", "n_gpus": world, "steps": steps,
@@ -1093,7 +1096,8 @@ def main_reference(args, wl, steps):
         "data": "synthetic (N(0,1) bf16-rounded, numpy generator seeded 0)",
         "config": config_of(wl, world, args.workload),
         "cpu_baseline": {"value": round(val, 6), "unit": unit, "cores": cores, "kind": "port",
-                         "sample": sample + f"; {n_run} of {total} requested steps run (bounded)"},
+                         "sample": sample + f"; a step is {blocks} such blocks; {warm} warm-up step(s) untimed, "
+                                   f"{n_timed} of {steps} requested steps timed (bounded)"},
         "e2e": {"value": round(val, 6), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

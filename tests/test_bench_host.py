@@ -171,3 +171,18 @@ def test_fp32_attention_checker_matches_the_oracle(bench):
     q, k, v = _rows_setup(seed=3, Sq=20, Skv=50)
     ref = T.gqa_reference_blocked(q, k, v, causal=True)
     assert torch.allclose(bench.fp32_attention(q, k, v), ref, atol=1e-6, rtol=1e-5)
+
+
+def test_reference_arm_line(bench, capsys, monkeypatch):
+    """--impl reference prints one line with the GPU line's config, its CPU sample and an
+    e2e that moves no bytes; warm-up steps are not timed."""
+    import argparse
+    import json
+    monkeypatch.delenv("RANK", raising=False)
+    monkeypatch.delenv("WORLD_SIZE", raising=False)
+    args = argparse.Namespace(workload="decode", warmup=3)
+    bench.main_reference(args, bench.WORKLOADS["decode"], 3)
+    line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and line["value"] > 0 and line["unit"] == "GB/s"
+    assert line["config"] == bench.config_of(bench.WORKLOADS["decode"], 1, "decode")
+    assert line["e2e"]["h2d_bytes_per_step"] == 0 and "warm-up step(s) untimed" in line["cpu_baseline"]["sample"]
