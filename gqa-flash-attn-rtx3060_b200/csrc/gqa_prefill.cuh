@@ -538,7 +538,12 @@ __global__ void __launch_bounds__(384, 1)
           sum2[c & 3] = add2(sum2[c & 3], pv);
           pk[c] = pack2<BF16>(pv.x, pv.y);
         }
-        if constexpr (kPairs == 32) tmem_st32(tS + 32 * h, pk); else tmem_st16(tS + 16 * h, pk);
+        if constexpr (kPairs >= 32) {
+#pragma unroll
+          for (int q = 0; q < kPairs / 32; ++q) tmem_st32(tS + kPairs * h + 32 * q, pk + 32 * q);
+        } else {
+          tmem_st16(tS + 16 * h, pk);
+        }
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(p_full + 8 * h);
