@@ -234,14 +234,15 @@ def paged_kv_append(key, value, key_cache, value_cache, slot_mapping, k_scale=1.
 
 @dataclass
 class PagedAttentionMetadata:
-    """The per-step metadata PagedAttention.forward reads (vLLM's attention metadata,
-    restricted to one new-token count per sequence).
+    """The per-step metadata PagedAttention.forward reads (vLLM's attention metadata).
 
     slot_mapping: int64 (num_tokens,), the cache slot of every new token (-1: padding).
     block_tables: int32 (num_seqs, max_blocks_per_seq).
     seq_lens: int32 (num_seqs,), keys per sequence after this step's tokens are appended.
-    query_len: new tokens per sequence (1 for decode); num_tokens = num_seqs * query_len,
-        the tokens ordered by sequence.
+    query_len: new tokens per sequence when every sequence has the same count (1 for
+        decode); num_tokens = num_seqs * query_len, the tokens ordered by sequence.
+    query_lens: for a mixed batch (chunked prefills and decodes together), the host list
+        of new tokens per sequence, tokens ordered by sequence; overrides query_len.
     max_seq_len: an upper bound of seq_lens (plans the key split); None: the block
         tables' capacity.
     """
@@ -250,6 +251,7 @@ class PagedAttentionMetadata:
     seq_lens: torch.Tensor
     query_len: int = 1
     max_seq_len: int = None
+    query_lens: list = None
 
 
 class PagedAttention:
@@ -299,17 +301,48 @@ class PagedAttention:
         k = key.view(num_tokens, self.num_kv_heads, self.head_size)
         v = value.view(num_tokens, self.num_kv_heads, self.head_size)
         key_cache, value_cache = kv_cache[0], kv_cache[1]
-        paged_kv_append(k, v, key_cache, value_cache, md.slot_mapping, self.k_scale, self.v_scale)
         num_seqs = md.seq_lens.shape[0]
-        if num_seqs * md.query_len != num_tokens:
-            raise ValueError("num_tokens must be num_seqs * query_len (one new-token count per sequence)")
-        if md.query_len == 1 and key_cache.dtype != torch.float8_e4m3fn:
-            out = paged_decode(q, key_cache, value_cache, md.block_tables, md.seq_lens, md.max_seq_len, self.scale)
-        else:
-            out = torch.empty((num_tokens, self.num_heads, self.head_size), dtype=query.dtype, device=query.device)
-            # tokens are ordered by sequence: (num_seqs, query_len, H, D) viewed as (num_seqs, H, query_len, D)
-            qv = q.view(num_seqs, md.query_len, self.num_heads, self.head_size).transpose(1, 2)
-            ov = out.view(num_seqs, md.query_len, self.num_heads, self.head_size).transpose(1, 2)
-            paged_prefill(qv, key_cache, value_cache, md.block_tables, md.seq_lens, md.max_seq_len, self.scale,
-                          causal=self.causal, k_scale=self.k_scale, v_scale=self.v_scale, out=ov)
+        lens = None if md.query_lens is None else [int(x) for x in md.query_lens]
+        if lens is not None:
+            if len(lens) != num_seqs or sum(lens) != num_tokens or min(lens, default=0) < 0:
+                raise ValueError("query_lens must give each sequence's new tokens, summing to num_tokens")
+        elif num_seqs * md.query_len != num_tokens:
+            raise ValueError("num_tokens must be num_seqs * query_len (or pass query_lens)")
+        paged_kv_append(k, v, key_cache, value_cache, md.slot_mapping, self.k_scale, self.v_scale)
+        if lens is None or len(set(lens)) == 1:
+            query_len = md.query_len if lens is None else lens[0]
+            out = self._attend(q, key_cache, value_cache, md.block_tables, md.seq_lens, md.max_seq_len, query_len)
+            return out.view(shape)
+        # Mixed batch: the kernels take one chunk length per call, so the sequences are
+        # grouped by their new-token count, each group attends in one call, and the rows
+        # are gathered from and scattered back to their places in the token order.
+        out = torch.empty((num_tokens, self.num_heads, self.head_size), dtype=query.dtype, device=query.device)
+        starts = [0]
+        for n in lens:
+            starts.append(starts[-1] + n)
+        groups = {}
+        for i, n in enumerate(lens):
+            if n:
+                groups.setdefault(n, []).append(i)
+        for n, seqs in groups.items():
+            rows = torch.tensor([starts[i] + t for i in seqs for t in range(n)], dtype=torch.int64,
+                                device=query.device)
+            sel = torch.tensor(seqs, dtype=torch.int64, device=query.device)
+            og = self._attend(q.index_select(0, rows), key_cache, value_cache, md.block_tables.index_select(0, sel),
+                              md.seq_lens.index_select(0, sel), md.max_seq_len, n)
+            out.index_copy_(0, rows, og)
         return out.view(shape)
+
+    def _attend(self, q, key_cache, value_cache, block_tables, seq_lens, max_seq_len, query_len):
+        """Attention of num_seqs sequences with query_len new tokens each; q and the result
+        are (num_seqs * query_len, num_heads, head_size), tokens ordered by sequence."""
+        num_seqs = seq_lens.shape[0]
+        if query_len == 1 and key_cache.dtype != torch.float8_e4m3fn:
+            return paged_decode(q, key_cache, value_cache, block_tables, seq_lens, max_seq_len, self.scale)
+        out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+        # tokens are ordered by sequence: (num_seqs, query_len, H, D) viewed as (num_seqs, H, query_len, D)
+        qv = q.view(num_seqs, query_len, self.num_heads, self.head_size).transpose(1, 2)
+        ov = out.view(num_seqs, query_len, self.num_heads, self.head_size).transpose(1, 2)
+        paged_prefill(qv, key_cache, value_cache, block_tables, seq_lens, max_seq_len, self.scale,
+                      causal=self.causal, k_scale=self.k_scale, v_scale=self.v_scale, out=ov)
+        return out

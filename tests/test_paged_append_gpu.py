@@ -254,3 +254,45 @@ def test_paged_attention_layer_prefill_then_decode(kv_cache_dtype):
             ref = torch_reference(qs.float(), ks, vs, causal=True)
             got = out[rows].view(1, qlen, Hq, D).transpose(1, 2)
             compare(to_np(got), to_np(ref), BASELINE_TOL)
+
+
+def test_paged_attention_layer_mixed_batches():
+    """Mixed batches (vLLM's chunked prefill and decode in one step): three sequences with
+    different new-token counts per step, given as query_lens; each step appends, then
+    attends, and every sequence's rows match the fp32 reference over its own history."""
+    Hq, Hkv, D, bs = 32, 8, 128, 64
+    dt = torch.bfloat16
+    layer = PagedAttention(Hq, D, num_kv_heads=Hkv)
+    cache = layer.allocate_kv_cache(64, bs, dt, "cuda")
+    bt = torch.randperm(60, generator=torch.Generator().manual_seed(5))[:60].view(3, 20).to(torch.int32).cuda()
+    g = torch.Generator(device="cuda").manual_seed(13)
+    lens = [0, 0, 0]
+    hist_k, hist_v = [[], [], []], [[], [], []]
+    for step_lens in ([200, 500, 1000], [1, 1, 37], [5, 1, 1], [1, 64, 1]):
+        n = sum(step_lens)
+        q = torch.randn(n, Hq * D, generator=g, device="cuda").to(dt)
+        k = torch.randn(n, Hkv * D, generator=g, device="cuda").to(dt)
+        v = torch.randn(n, Hkv * D, generator=g, device="cuda").to(dt)
+        slots = []
+        for s, m in enumerate(step_lens):
+            for t in range(m):
+                pos = lens[s] + t
+                slots.append(int(bt[s, pos // bs]) * bs + pos % bs)
+            lens[s] += m
+        md = PagedAttentionMetadata(slot_mapping=torch.tensor(slots, dtype=torch.int64, device="cuda"),
+                                    block_tables=bt, seq_lens=torch.tensor(lens, dtype=torch.int32, device="cuda"),
+                                    query_lens=step_lens)
+        out = layer.forward(q, k, v, cache, md)
+        torch.cuda.synchronize()
+        assert out.shape == q.shape and torch.isfinite(out).all()
+        r0 = 0
+        for s, m in enumerate(step_lens):
+            rows = slice(r0, r0 + m)
+            r0 += m
+            hist_k[s].append(k[rows].view(m, Hkv, D))
+            hist_v[s].append(v[rows].view(m, Hkv, D))
+            ks = torch.cat(hist_k[s]).float().permute(1, 0, 2).unsqueeze(0)
+            vs = torch.cat(hist_v[s]).float().permute(1, 0, 2).unsqueeze(0)
+            qs = q[rows].view(1, m, Hq, D).transpose(1, 2).float()
+            ref = torch_reference(qs, ks, vs, causal=True)
+            compare(to_np(out[rows].view(1, m, Hq, D).transpose(1, 2)), to_np(ref), BASELINE_TOL)

@@ -140,3 +140,20 @@ def test_paged_attention_layer_arguments():
     layer = PagedAttention(32, 128, num_kv_heads=8, kv_cache_dtype="fp8_e4m3")
     cache = layer.allocate_kv_cache(4, 64, torch.bfloat16, "cpu")
     assert cache.shape == (2, 4, 64, 8, 128) and cache.dtype == torch.float8_e4m3fn
+
+
+def test_paged_attention_layer_rejects_inconsistent_query_lens():
+    from gqa_kernels.paged import PagedAttention, PagedAttentionMetadata
+    layer = PagedAttention(8, 64, num_kv_heads=2)
+    q = torch.zeros(5, 8 * 64, dtype=torch.bfloat16)
+    kv = torch.zeros(5, 2 * 64, dtype=torch.bfloat16)
+    cache = layer.allocate_kv_cache(4, 64, torch.bfloat16, "cpu")
+    md = PagedAttentionMetadata(slot_mapping=torch.zeros(5, dtype=torch.int64),
+                                block_tables=torch.zeros(2, 2, dtype=torch.int32),
+                                seq_lens=torch.tensor([3, 3], dtype=torch.int32), query_lens=[2, 2])
+    with pytest.raises(ValueError):
+        layer.forward(q, kv, kv, cache, md)  # 2 + 2 != 5 tokens
+    md.query_lens = None
+    md.query_len = 2
+    with pytest.raises(ValueError):
+        layer.forward(q, kv, kv, cache, md)  # 2 sequences x 2 != 5 tokens
