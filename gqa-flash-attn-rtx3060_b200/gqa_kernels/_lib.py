@@ -97,11 +97,11 @@ def check_one_device(*tensors):
     """Every tensor a launch reads or writes must be CUDA memory of one device: the
     kernels take raw pointers and run on the first tensor's device."""
     dev = tensors[0].device
+    if dev.type != "cuda":
+        raise ValueError("tensors must be on a CUDA device")
     for t in tensors:
-        if not t.is_cuda:
-            raise ValueError("tensors must be on a CUDA device")
         if t.device != dev:
-            raise ValueError("tensors must be on one device")
+            raise ValueError("tensors must be on one device" if t.is_cuda else "tensors must be on a CUDA device")
 
 
 _STRIDES = {}
@@ -171,11 +171,15 @@ def workspace_bytes(query, *shape):
 def tma_compatible(t):
     """True if `t` meets the library's layout rule: contiguous in the last dim,
     other strides multiples of 8 elements, base 16-byte aligned."""
-    if t.stride(-1) != 1 and t.shape[-1] != 1:
+    st = t.stride()
+    if st[-1] != 1 and t.shape[-1] != 1:
         return False
-    if t.data_ptr() % 16:
+    if t.data_ptr() & 15:
         return False
-    return all(s % 8 == 0 for s in t.stride()[:-1])
+    for s in st[:-1]:
+        if s & 7:
+            return False
+    return True
 
 
 class WorkspaceCache:
