@@ -1046,7 +1046,9 @@ def main():
             line["gpu_launches"] += launches
 
     if not args.no_e2e:
-        e2e = run_e2e(wl, world, rank, device, 20 if args.workload == "prefill" else 200, args)
+        # 60 prefill steps: the pipeline's fill (the first inputs' copy) and drain (the last
+        # output's copy) are not overlapped, so fewer steps would understate the steady state
+        e2e = run_e2e(wl, world, rank, device, 60 if args.workload == "prefill" else 200, args)
         if e2e is not None:
             line["e2e"] = e2e
 
