@@ -613,8 +613,11 @@ __global__ void __launch_bounds__(288, 1)
   GQA_CBAR();  // every compute warp is done with the ring
   // acc rows are padded to HD + 8 floats: the 8 row lanes of a float2 store then
   // start 8 banks apart and each store takes the minimum two wavefronts. Rows of
-  // the upper half of a row group are stored only when the unit has them.
-  constexpr int AS = HD + 8;
+  // the upper half of a row group are stored only when the unit has them. The
+  // transposed (decode) form stores scalars whose lanes span rows 2gc (gc = 0..3)
+  // and 8 consecutive d: a pad of HD + 4 puts those rows 8 banks apart, so each
+  // store is one wavefront (HD + 8 would put rows 0 and 4 on the same banks).
+  constexpr int AS = NT ? HD + 4 : HD + 8;
   float* mbuf = reinterpret_cast<float*>(smem);  // [NW][16]
   float* lbuf = mbuf + NW * 16;                  // [NW][16]
   float* abuf = lbuf + NW * 16;                  // [NW][16][AS]
@@ -840,28 +843,39 @@ __global__ void __launch_bounds__(288, 1)
     const int r = idx / per_row, d = (idx - r * per_row) * 4;
     const int g = r / p.block_m, m = r - g * p.block_m, pos = mt * p.block_m + m;
     if (pos >= p.seq_q) continue;
+    // Splits in batches of kCombBatch: every load of a batch is issued before the
+    // first FMA, so a batch costs one load latency instead of one per split. The
+    // sum runs in split order, as the reference's reduce does.
+    constexpr int kCombBatch = 8;
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    auto accumulate = [&](auto load) {
+      for (int s0 = 0; s0 < p.nsplit; s0 += kCombBatch) {
+        float wt[kCombBatch];
+        float4 v[kCombBatch];
+#pragma unroll
+        for (int u = 0; u < kCombBatch; ++u) {
+          if (s0 + u < p.nsplit) {
+            wt[u] = sm_w[(s0 + u) * n_rows + r];
+            v[u] = load(s0 + u);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kCombBatch; ++u) {
+          if (s0 + u < p.nsplit) {
+            a.x += wt[u] * v[u].x;
+            a.y += wt[u] * v[u].y;
+            a.z += wt[u] * v[u].z;
+            a.w += wt[u] * v[u].w;
+          }
+        }
+      }
+    };
     if (staged) {
-#pragma unroll 4
-      for (int s2 = 0; s2 < p.nsplit; ++s2) {
-        const float wt = sm_w[s2 * n_rows + r];
-        const float4 v = *reinterpret_cast<const float4*>(cacc + (s2 * n_rows + r) * HD + d);
-        a.x += wt * v.x;
-        a.y += wt * v.y;
-        a.z += wt * v.z;
-        a.w += wt * v.w;
-      }
+      accumulate([&](int s2) { return *reinterpret_cast<const float4*>(cacc + (s2 * n_rows + r) * HD + d); });
     } else {
-#pragma unroll 8
-      for (int s2 = 0; s2 < p.nsplit; ++s2) {
-        const float wt = sm_w[s2 * n_rows + r];
-        const float4 v =
-            __ldcg(reinterpret_cast<const float4*>(p.ws_acc + (ubase + (int64_t)s2 * p.rows + r) * HD + d));
-        a.x += wt * v.x;
-        a.y += wt * v.y;
-        a.z += wt * v.z;
-        a.w += wt * v.w;
-      }
+      accumulate([&](int s2) {
+        return __ldcg(reinterpret_cast<const float4*>(p.ws_acc + (ubase + (int64_t)s2 * p.rows + r) * HD + d));
+      });
     }
     const int head = kvh * p.group + g;
     if (p.mode == kStreamFused) {
