@@ -621,7 +621,7 @@ __global__ void __launch_bounds__(288, 1)
   float* mbuf = reinterpret_cast<float*>(smem);  // [NW][16]
   float* lbuf = mbuf + NW * 16;                  // [NW][16]
   float* abuf = lbuf + NW * 16;                  // [NW][16][AS]
-  static_assert((2 * NW * 16 + NW * 16 * AS + 128 + 64 * KS) * 4 <= Cfg::kRingBytes, "merge buffers fit the ring");
+  static_assert((2 * NW * 16 + NW * 16 * AS) * 4 <= Cfg::kRingBytes, "merge buffers fit the ring");
   {
     float* aw = abuf + warp * 16 * AS;
     const bool upper = rg * 16 + 8 < p.rows;  // warp-uniform
@@ -682,44 +682,38 @@ __global__ void __launch_bounds__(288, 1)
   }
   GQA_CBAR();
 
-  // Combined per-row (M, L) of this CTA and the per-warp weights.
-  float* fin_m = abuf + NW * 16 * AS;  // [64]
-  float* fin_l = fin_m + 64;           // [64]
-  float* fin_w = fin_l + 64;           // [64][KS]
-  if (tid < RG * 16) {
-    const int r = tid;
+  // This CTA's combined (M, L) of packed row r and its acc over columns d..d+3,
+  // from the KS warps' partials of the row. Every thread that writes a row computes
+  // the row's weights itself (KS loads and exp2s, the same values in the same order
+  // for all of them): no barrier and no separate weights phase between the stores
+  // above and the writes below.
+  struct RowMerge {
+    float M, L;
+    float4 a;
+  };
+  auto merge_row = [&](int r, int d) {
     const int g_rg = r / 16, rr = r % 16;
+    float mk[KS];
     float M = -INFINITY;
 #pragma unroll
-    for (int k2 = 0; k2 < KS; ++k2) M = fmaxf(M, mbuf[(k2 * RG + g_rg) * 16 + rr]);
+    for (int k2 = 0; k2 < KS; ++k2) {
+      mk[k2] = mbuf[(k2 * RG + g_rg) * 16 + rr];
+      M = fmaxf(M, mk[k2]);
+    }
     const float Mu = (M == -INFINITY) ? 0.f : M;
-    float L = 0.f;
+    RowMerge out{M, 0.f, make_float4(0.f, 0.f, 0.f, 0.f)};
 #pragma unroll
     for (int k2 = 0; k2 < KS; ++k2) {
       const int w = k2 * RG + g_rg;
-      const float wt = fast_exp2(mbuf[w * 16 + rr] - Mu);
-      fin_w[r * KS + k2] = wt;
-      L += wt * lbuf[w * 16 + rr];
+      const float wt = fast_exp2(mk[k2] - Mu);
+      out.L += wt * lbuf[w * 16 + rr];
+      const float4 v = *reinterpret_cast<const float4*>(abuf + (w * 16 + rr) * AS + d);
+      out.a.x += wt * v.x;
+      out.a.y += wt * v.y;
+      out.a.z += wt * v.z;
+      out.a.w += wt * v.w;
     }
-    fin_m[r] = M;
-    fin_l[r] = L;
-  }
-  GQA_CBAR();
-
-  // This CTA's combined acc for packed row r, columns d..d+3.
-  auto cta_acc = [&](int r, int d) {
-    const int g_rg = r / 16, rr = r % 16;
-    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int k2 = 0; k2 < KS; ++k2) {
-      const float wt = fin_w[r * KS + k2];
-      const float4 v = *reinterpret_cast<const float4*>(abuf + ((k2 * RG + g_rg) * 16 + rr) * AS + d);
-      a.x += wt * v.x;
-      a.y += wt * v.y;
-      a.z += wt * v.z;
-      a.w += wt * v.w;
-    }
-    return a;
+    return out;
   };
 
   const int n_rows = min(p.rows, RG * 16);
@@ -729,8 +723,9 @@ __global__ void __launch_bounds__(288, 1)
       const int r = idx / per_row, d = (idx - r * per_row) * 4;
       const int g = r / p.block_m, m = r - g * p.block_m, pos = mt * p.block_m + m;
       if (pos >= p.seq_q) continue;
-      const float4 a = cta_acc(r, d);
-      const float inv = 1.f / fin_l[r];  // l == 0 (no visible key) -> NaN, as the reference
+      const RowMerge mr = merge_row(r, d);
+      const float4 a = mr.a;
+      const float inv = 1.f / mr.L;  // l == 0 (no visible key) -> NaN, as the reference
       uint2 pk;
       pk.x = pack2<BF16>(a.x * inv, a.y * inv);
       pk.y = pack2<BF16>(a.z * inv, a.w * inv);
@@ -746,7 +741,8 @@ __global__ void __launch_bounds__(288, 1)
       const int g = r / p.block_m, m = r - g * p.block_m, pos = mt * p.block_m + m;
       if (pos >= p.seq_q) continue;
       const int head = kvh * p.group + g;
-      const float4 a = cta_acc(r, d);
+      const RowMerge mr = merge_row(r, d);
+      const float4 a = mr.a;
       float* ap = p.acc_p + b * p.a_sb + head * p.a_sh + (int64_t)pos * p.a_sm + (int64_t)split * p.a_ss;
       ap[(int64_t)(d + 0) * p.a_sd] = a.x;
       ap[(int64_t)(d + 1) * p.a_sd] = a.y;
@@ -754,8 +750,8 @@ __global__ void __launch_bounds__(288, 1)
       ap[(int64_t)(d + 3) * p.a_sd] = a.w;
       if (d == 0) {
         const int64_t po = b * p.p_sb + head * p.p_sh + (int64_t)pos * p.p_sm + (int64_t)split * p.p_ss;
-        p.m_p[po] = fin_m[r];
-        p.l_p[po] = fin_l[r];
+        p.m_p[po] = mr.M;
+        p.l_p[po] = mr.L;
       }
     }
     return;
@@ -765,10 +761,11 @@ __global__ void __launch_bounds__(288, 1)
   const int64_t wbase = ((int64_t)unit * p.nsplit + split) * p.rows;
   for (int idx = tid; idx < n_rows * per_row; idx += CT) {
     const int r = idx / per_row, d = (idx - r * per_row) * 4;
-    __stcg(reinterpret_cast<float4*>(p.ws_acc + (wbase + r) * HD + d), cta_acc(r, d));
+    const RowMerge mr = merge_row(r, d);
+    __stcg(reinterpret_cast<float4*>(p.ws_acc + (wbase + r) * HD + d), mr.a);
     if (d == 0) {
-      __stcg(p.ws_m + wbase + r, fin_m[r]);
-      __stcg(p.ws_l + wbase + r, fin_l[r]);
+      __stcg(p.ws_m + wbase + r, mr.M);
+      __stcg(p.ws_l + wbase + r, mr.L);
     }
   }
   // The CTA barrier orders every thread's partial stores before thread 0's
