@@ -189,6 +189,11 @@ def dist_setup(n_gpus):
         import torch.distributed as dist
         torch.cuda.set_device(local)
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        # NCCL's init lines (communicator rank count and topology, on stderr) stay on,
+        # so the run's log shows how many ranks each communicator had. The INIT
+        # subsystem only, to keep the log short; a caller's own setting wins.
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=torch.device("cuda", local))
     elif n_gpus > 1:
