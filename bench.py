@@ -189,11 +189,6 @@ def dist_setup(n_gpus):
         import torch.distributed as dist
         torch.cuda.set_device(local)
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        # NCCL's init lines (communicator rank count and topology, on stderr) stay on,
-        # so the run's log shows how many ranks each communicator had. The INIT
-        # subsystem only, to keep the log short; a caller's own setting wins.
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=torch.device("cuda", local))
     elif n_gpus > 1:
@@ -684,6 +679,15 @@ def run_attention_workload(wl, world, rank, device, steps, warmup, args):
     if name in ("decode", "paged_decode", "paged_decode_fp8"):
         graph_of(16), graph_of(steps % 16 or 16)  # capture outside the timed region
         times, wall = timed_loop(step, steps, warmup, world, device)
+    elif name == "long_decode":
+        # K/V far larger than L2 at every N (4.3 GB per rank at N = 8), so no flush:
+        # the steps run back to back as a decode loop issues them, between one
+        # barrier-and-synchronize pair, and each rank's host jitter is not inside
+        # every step's all-gather
+        def run_steps(n):
+            for i in range(n):
+                step(i)
+        times, wall = timed_loop(run_steps, steps, warmup, world, device)
     else:
         times, wall = timed_steps(step, steps, warmup, world, device, flush=flush)
     clocks = clock.stop() if clock else None
