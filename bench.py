@@ -81,7 +81,7 @@ WORKLOADS = {
     "chunked": dict(B=4, Hq=32, Hkv=8, Sq=512, Skv=16384, D=128, bound="tensor", scaling="strong",
                     name="chunked-prefill-b4-512x16k (config 4), batch x kv-head sharded"),
     "long_decode": dict(B=64, Hq=64, Hkv=8, Sq=1, Skv=131072, D=128, bound="hbm", scaling="strong",
-                        name="long-decode-b64-131k (config 5), seq_kv sharded + NCCL LSE combine"),
+                        name="long-decode-b64-131k (config 5), seq_kv sharded + LSE combine"),
     # Paged-cache decode (gqa_kernels.paged): config 3's shape for 8 sequences, vLLM
     # cache layout with 256-key blocks in shuffled order; bf16 or e4m3 K/V.
     "paged_decode": dict(B=8, Hq=32, Hkv=8, Sq=1, Skv=16384, D=128, bound="hbm", scaling="weak", kv="bf16",
@@ -661,14 +661,25 @@ def run_attention_workload(wl, world, rank, device, steps, warmup, args):
         elif args.impl != "ours":
             raise SystemExit("the library comparators run the seq_kv-sharded workload on one GPU only")
         else:
-            packed = torch.empty(S.packed_size(q.shape), dtype=torch.float32, device=device)
-            gathered = torch.empty((world, packed.numel()), dtype=torch.float32, device=device)
+            if args.exchange == "peer" and S.all_shards_hold_keys(Skv, world):
+                # the partial kernel stores its rows into every rank's buffer over
+                # NVLink; each rank's combine waits for them in the kernel
+                ex = S.PeerExchange(q.shape, Hkv, device)
+                o_buf = torch.empty_like(q)
+                local["exchange"] = ex
 
-            def step(i):
-                S.partial_forward(q, k, v, True, k0, Skv, out=packed)
-                S.gather_partials(packed, out=gathered)
-                local["o"] = S.combine_partials(gathered, tuple(q.shape), dt, device)
-            launches_per_step = 2
+                def step(i):
+                    local["o"] = ex.forward(q, k, v, k0, Skv, out=o_buf)
+                launches_per_step = 3
+            else:
+                packed = torch.empty(S.packed_size(q.shape), dtype=torch.float32, device=device)
+                gathered = torch.empty((world, packed.numel()), dtype=torch.float32, device=device)
+
+                def step(i):
+                    S.partial_forward(q, k, v, True, k0, Skv, out=packed)
+                    S.gather_partials(packed, out=gathered)
+                    local["o"] = S.combine_partials(gathered, tuple(q.shape), dt, device)
+                launches_per_step = 2
         flush = None
     else:
         raise SystemExit(f"unknown workload {name}")
@@ -872,7 +883,7 @@ def cpu_sample(wl, budget_s, steps=None, kind="torch"):
     return val, unit, sample, per, cores
 
 
-def config_of(wl, world, workload):
+def config_of(wl, world, workload, exchange="nccl"):
     """The `config` of a bench line; the reference arm prints the same dict."""
     return {"workload": wl["name"], "batch_per_gpu" if wl["scaling"] == "weak" else "batch": wl["B"],
             "num_heads": wl["Hq"], "num_kv_heads": wl["Hkv"], "seq_q": wl["Sq"], "seq_kv": wl["Skv"],
@@ -885,7 +896,9 @@ def config_of(wl, world, workload):
             else "inputs larger than L2 (32 GiB K/V)",
             "parallelism": (f"batch-sharded x{world}" if wl["scaling"] == "weak" else
                             f"kv-head/batch x{world}" if workload == "chunked" else
-                            f"seq_kv x{world} + NCCL all-gather LSE combine")}
+                            f"seq_kv x{world} + " + ("peer-exchange LSE combine (partials stored over NVLink by the "
+                                                     "partial kernel, in-kernel waits in the combine)"
+                                                     if exchange == "peer" else "NCCL all-gather LSE combine"))}
 
 
 def roofline_of(wl, res, world, peaks, workload):
@@ -918,18 +931,25 @@ def sharded_object(key, args, world, rank, device, peaks, comparator):
     sargs = argparse.Namespace(**{**vars(args), "workload": wname})
     res = run_attention_workload(swl, world, rank, device, nsteps, args.warmup, sargs)
     par = parity_check(res["local"], world, sharded_keys=(wname == "long_decode"))
+    ex = res["local"].pop("exchange", None)
+    exchange = "peer" if ex is not None else "nccl"
+    if ex is not None:
+        ex.close()  # collective: every rank reaches it after the same steps
     res["local"].clear()
     torch.cuda.empty_cache()
     peak = peaks["bf16"] if swl["bound"] == "tensor" else peaks["hbm"]
     obj = {"value": round(res["value"], 3), "unit": res["unit"], "ms_per_step": round(res["ms_per_step"], 5),
            "steps": nsteps, "scaling": swl["scaling"], "n_gpus": world,
            "frac_of_n_peak": round(res["value"] / (world * peak), 4),
-           "config": config_of(swl, world, wname), "roofline": roofline_of(swl, res, world, peaks, wname),
+           "config": config_of(swl, world, wname, exchange if world > 1 else "nccl"),
+           "roofline": roofline_of(swl, res, world, peaks, wname),
            "parity": par, "clocks": res["clocks"]}
     if world > 1:
         import torch.distributed as dist
         obj["nccl"] = {"backend": dist.get_backend(), "ranks": dist.get_world_size(),
-                       "collectives_per_step": 1 if wname == "long_decode" else 0}
+                       "collectives_per_step": 1 if (wname == "long_decode" and exchange == "nccl") else 0}
+        if wname == "long_decode":
+            obj["exchange"] = exchange
     return obj, (0 if comparator else res["launches"])
 
 
@@ -950,6 +970,8 @@ def main():
     ap.add_argument("--decode-steps", type=int, default=5000, help="timed steps of the decode half")
     ap.add_argument("--chunked-steps", type=int, default=200, help="timed steps of the config-4 object")
     ap.add_argument("--long-steps", type=int, default=40, help="timed steps of the config-5 object")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="config 5 at N>1: partials stored over NVLink by the kernels, or one NCCL all-gather")
     ap.add_argument("--sweep", action="store_true",
                     help="the reference harness on this box (benchmark/run.py): correctness gate of this library, "
                          "SDPA and flash_attn, then the prefill/decode sweep; prints a table, writes --results")
@@ -1021,6 +1043,10 @@ def main():
     line["clocks"] = res["clocks"]
     if res["local"]:
         line["parity"] = parity_check(res["local"], world, sharded_keys=(args.workload == "long_decode"))
+    ex = res["local"].pop("exchange", None)
+    if ex is not None:
+        line["config"] = config_of(wl, world, args.workload, "peer")
+        ex.close()  # collective: every rank reaches it after the same steps
     res["local"].clear()
 
     # decode half of the headline metric

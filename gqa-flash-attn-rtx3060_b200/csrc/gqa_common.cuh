@@ -38,6 +38,17 @@ __device__ __forceinline__ void report_device_error(int code, int site) {
   if (atomicCAS(&g_device_error, 0, code) == 0) g_device_error_site = site;
 }
 
+// Ranks of one peer exchange: the GPUs of one node.
+constexpr int kMaxPeers = 8;
+
+// System-scope acquire load: orders this thread's later reads after the writes
+// (from any GPU) that a matching release made visible.
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 #ifdef GQA_DEBUG_CHECKS
 // Test hooks of the checked build (gqa_debug_inject): the wait limit can be
 // shortened at run time, and the TMA producer of one CTA can withhold one of its

@@ -3,7 +3,9 @@
 // Validates arguments (returning GQA_ERR_* before any launch), builds the TMA
 // tensor maps, sizes the launch for the current device's SM count and
 // enqueues the kernels on the caller's stream. Nothing here allocates device
-// memory or synchronises (except gqa_device_error, which says so).
+// memory or synchronises (except gqa_device_error and the peer exchange's setup
+// calls, gqa_exchange_alloc / gqa_ipc_*, which say so).
+#include <cstring>
 #include <mutex>
 #include <utility>
 #include <vector>
@@ -784,9 +786,14 @@ int gqa_split_first(const void* q, const void* k, const void* v, float* m_p, flo
   return run_stream(s, pl, p, k, v, ks, vs, dtype, reinterpret_cast<cudaStream_t>(stream));
 }
 
-int gqa_split_reduce(const float* m_p, const float* l_p, const float* acc_p, void* o, const int64_t* ps,
-                     const int64_t* as, const int64_t* os, int batch, int num_heads, int seq_q, int head_dim,
-                     int splits, int dtype, void* stream) {
+}  // extern "C"
+
+namespace {
+// gqa_split_reduce's checks and launch; `peer` adds the peer exchange's wait
+// (counters, epoch, units per source, parity stride) to the combine.
+int split_reduce_impl(const float* m_p, const float* l_p, const float* acc_p, void* o, const int64_t* ps,
+                      const int64_t* as, const int64_t* os, int batch, int num_heads, int seq_q, int head_dim,
+                      int splits, int dtype, void* stream, const CombineParams* peer) {
   if (!m_p || !l_p || !acc_p || !o || !ps || !as || !os) return GQA_ERR_INVALID_ARG;
   if (batch < 0 || num_heads <= 0 || seq_q < 0 || splits <= 0) return GQA_ERR_INVALID_ARG;
   if (head_dim != 64 && head_dim != 128) return GQA_ERR_UNSUPPORTED;
@@ -803,6 +810,12 @@ int gqa_split_reduce(const float* m_p, const float* l_p, const float* acc_p, voi
   p.a_sb = as[0]; p.a_sh = as[1]; p.a_sm = as[2]; p.a_ss = as[3]; p.a_sd = as[4];
   p.o_sb = os[0]; p.o_sh = os[1]; p.o_sm = os[2];
   p.batch = batch; p.hq = num_heads; p.seq_q = seq_q; p.head_dim = head_dim; p.nsplit = splits;
+  if (peer) {
+    p.cnt = peer->cnt;
+    p.epoch = peer->epoch;
+    p.units = peer->units;
+    p.parity_stride = peer->parity_stride;
+  }
   const int64_t rows = (int64_t)batch * num_heads * seq_q;
   const int64_t blocks = (rows + 3) / 4;
   if (blocks > 0x7fffffff) return GQA_ERR_INVALID_ARG;
@@ -812,6 +825,16 @@ int gqa_split_reduce(const float* m_p, const float* l_p, const float* acc_p, voi
   else
     gqa_combine_kernel<false><<<(unsigned)blocks, 128, 0, st>>>(p);
   return launch_status();
+}
+}  // namespace
+
+extern "C" {
+
+int gqa_split_reduce(const float* m_p, const float* l_p, const float* acc_p, void* o, const int64_t* ps,
+                     const int64_t* as, const int64_t* os, int batch, int num_heads, int seq_q, int head_dim,
+                     int splits, int dtype, void* stream) {
+  return split_reduce_impl(m_p, l_p, acc_p, o, ps, as, os, batch, num_heads, seq_q, head_dim, splits, dtype, stream,
+                           nullptr);
 }
 
 size_t gqa_split_fused_workspace_bytes(int batch, int num_heads, int num_kv_heads, int seq_q, int seq_kv,
@@ -941,22 +964,35 @@ size_t gqa_partial_workspace_bytes(int batch, int num_heads, int num_kv_heads, i
   return stream_ws_bytes(plan_stream(s, sm, true), head_dim);
 }
 
-int gqa_partial(const void* q, const void* k, const void* v, float* m_out, float* l_out, float* acc_out,
-                const int64_t* qs, const int64_t* ks, const int64_t* vs, int batch, int num_heads, int num_kv_heads,
-                int seq_q, int seq_kv_local, int kv_offset, int seq_kv_total, int head_dim, float scale_log2,
-                int causal, int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+// The peer-exchange outputs of gqa_partial_peer (nullptr: gqa_partial's own arrays).
+struct PeerArgs {
+  float* const* bases;
+  unsigned long long* const* cnts;
+  int npeer, rank;
+  const unsigned long long* epoch;
+  int64_t slot, parity;
+};
+
+int partial_impl(const void* q, const void* k, const void* v, float* m_out, float* l_out, float* acc_out,
+                 const int64_t* qs, const int64_t* ks, const int64_t* vs, int batch, int num_heads, int num_kv_heads,
+                 int seq_q, int seq_kv_local, int kv_offset, int seq_kv_total, int head_dim, float scale_log2,
+                 int causal, int dtype, void* workspace, size_t workspace_bytes, void* stream, const PeerArgs* peer) {
   Shape s;
   int rc = check_shape(batch, num_heads, num_kv_heads, seq_q, seq_kv_local, head_dim, &s);
   if (rc) return rc;
-  if (!m_out || !l_out || !acc_out) return GQA_ERR_INVALID_ARG;
+  if (!peer && (!m_out || !l_out || !acc_out)) return GQA_ERR_INVALID_ARG;
   if (kv_offset < 0 || seq_kv_total < kv_offset + seq_kv_local) return GQA_ERR_INVALID_ARG;
   if (batch == 0 || seq_q == 0) return GQA_OK;
   if (s.group > kStreamMaxRows) return GQA_ERR_UNSUPPORTED;
   if (dtype != GQA_DTYPE_BF16 && dtype != GQA_DTYPE_F16) return GQA_ERR_UNSUPPORTED;
-  if (!aligned16(acc_out)) return GQA_ERR_ALIGNMENT;
+  if (!peer && !aligned16(acc_out)) return GQA_ERR_ALIGNMENT;
   int sm = 0;
   rc = current_device(&sm);
   if (rc) return rc;
+  if (peer && seq_kv_local == 0) return GQA_ERR_UNSUPPORTED;  // every rank must hold keys
   if (seq_kv_local == 0) {
     // An empty shard (more ranks than 64-key blocks) is a valid part: (-inf, 0, 0)
     // for every row, which the combine weighs 0. k and v may have no storage.
@@ -980,8 +1016,34 @@ int gqa_partial(const void* q, const void* k, const void* v, float* m_out, float
   p.seq_kv_total = seq_kv_total;
   p.mode = kStreamFusedPartial;
   p.m_out = m_out; p.l_out = l_out; p.acc_out = acc_out;
+  if (peer) {
+    const int64_t rows = (int64_t)batch * num_heads * seq_q;
+    p.npeer = peer->npeer;
+    p.my_rank = peer->rank;
+    for (int i = 0; i < peer->npeer; ++i) {
+      p.peer_base[i] = peer->bases[i];
+      p.peer_cnt[i] = peer->cnts[i];
+    }
+    p.epoch = peer->epoch;
+    p.peer_slot = peer->slot;
+    p.peer_parity = peer->parity;
+    p.pk_rows = rows;
+    p.pk_acc = (2 * rows + 3) / 4 * 4;
+  }
   stream_ws_carve(pl, head_dim, workspace, &p);
   return run_stream(s, pl, p, k, v, ks, vs, dtype, reinterpret_cast<cudaStream_t>(stream));
+}
+}  // namespace
+
+extern "C" {
+
+int gqa_partial(const void* q, const void* k, const void* v, float* m_out, float* l_out, float* acc_out,
+                const int64_t* qs, const int64_t* ks, const int64_t* vs, int batch, int num_heads, int num_kv_heads,
+                int seq_q, int seq_kv_local, int kv_offset, int seq_kv_total, int head_dim, float scale_log2,
+                int causal, int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  return partial_impl(q, k, v, m_out, l_out, acc_out, qs, ks, vs, batch, num_heads, num_kv_heads, seq_q, seq_kv_local,
+                      kv_offset, seq_kv_total, head_dim, scale_log2, causal, dtype, workspace, workspace_bytes, stream,
+                      nullptr);
 }
 
 int gqa_lse_combine(const float* m_parts, const float* l_parts, const float* acc_parts, int nparts,
@@ -994,6 +1056,100 @@ int gqa_lse_combine(const float* m_parts, const float* l_parts, const float* acc
                          acc_part_stride, 1};
   return gqa_split_reduce(m_parts, l_parts, acc_parts, o, ps, as, os, batch, num_heads, seq_q, head_dim, nparts,
                           dtype, stream);
+}
+
+// ---- peer exchange (key-sharded multi-GPU combine without a collective library)
+static_assert(sizeof(cudaIpcMemHandle_t) == GQA_IPC_HANDLE_BYTES, "IPC handle size");
+
+int gqa_exchange_alloc(size_t bytes, void** ptr) {
+  if (!ptr || bytes == 0) return GQA_ERR_INVALID_ARG;
+  int rc = current_device(nullptr);
+  if (rc) return rc;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return GQA_ERR_CUDA;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess) {
+    cudaFree(p);
+    return GQA_ERR_CUDA;
+  }
+  *ptr = p;
+  return GQA_OK;
+}
+
+int gqa_exchange_free(void* ptr) { return (!ptr || cudaFree(ptr) == cudaSuccess) ? GQA_OK : GQA_ERR_CUDA; }
+
+int gqa_ipc_handle(const void* ptr, void* handle) {
+  if (!ptr || !handle) return GQA_ERR_INVALID_ARG;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, const_cast<void*>(ptr)) != cudaSuccess) return GQA_ERR_CUDA;
+  std::memcpy(handle, &h, sizeof(h));
+  return GQA_OK;
+}
+
+int gqa_ipc_open(const void* handle, void** ptr) {
+  if (!handle || !ptr) return GQA_ERR_INVALID_ARG;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  if (cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return GQA_ERR_CUDA;
+  return GQA_OK;
+}
+
+int gqa_ipc_close(void* ptr) { return (ptr && cudaIpcCloseMemHandle(ptr) == cudaSuccess) ? GQA_OK : GQA_ERR_CUDA; }
+
+int gqa_epoch_bump(unsigned long long* epoch, void* stream) {
+  if (!epoch) return GQA_ERR_INVALID_ARG;
+  gqa_epoch_bump_kernel<<<1, 1, 0, reinterpret_cast<cudaStream_t>(stream)>>>(epoch);
+  return launch_status();
+}
+
+int gqa_partial_units(int batch, int num_heads, int num_kv_heads, int seq_q, int head_dim, int* units) {
+  if (!units) return GQA_ERR_INVALID_ARG;
+  Shape s;
+  const int rc = check_shape(batch, num_heads, num_kv_heads, seq_q, 1, head_dim, &s);
+  if (rc) return rc;
+  *units = (batch == 0 || seq_q == 0) ? 0 : plan_stream(s, 1, false).units;
+  return GQA_OK;
+}
+
+int gqa_partial_peer(const void* q, const void* k, const void* v, const int64_t* qs, const int64_t* ks,
+                     const int64_t* vs, int batch, int num_heads, int num_kv_heads, int seq_q, int seq_kv_local,
+                     int kv_offset, int seq_kv_total, int head_dim, float scale_log2, int causal, int dtype,
+                     float* const* peer_bases, unsigned long long* const* peer_cnts, int npeer, int rank,
+                     const unsigned long long* epoch, int64_t slot_floats, int64_t parity_floats, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  if (!peer_bases || !peer_cnts || !epoch || npeer < 1 || npeer > kMaxPeers || rank < 0 || rank >= npeer)
+    return GQA_ERR_INVALID_ARG;
+  const int64_t rows = (int64_t)batch * num_heads * seq_q;
+  const int64_t packed = (2 * rows + 3) / 4 * 4 + rows * head_dim;
+  if (slot_floats < packed || parity_floats < npeer * slot_floats) return GQA_ERR_INVALID_ARG;
+  if (slot_floats % 4 || parity_floats % 4) return GQA_ERR_ALIGNMENT;
+  for (int i = 0; i < npeer; ++i) {
+    if (!peer_bases[i] || !peer_cnts[i]) return GQA_ERR_INVALID_ARG;
+    if (!aligned16(peer_bases[i]) || (reinterpret_cast<uintptr_t>(peer_cnts[i]) & 7u)) return GQA_ERR_ALIGNMENT;
+  }
+  const PeerArgs pa{peer_bases, peer_cnts, npeer, rank, epoch, slot_floats, parity_floats};
+  return partial_impl(q, k, v, nullptr, nullptr, nullptr, qs, ks, vs, batch, num_heads, num_kv_heads, seq_q,
+                      seq_kv_local, kv_offset, seq_kv_total, head_dim, scale_log2, causal, dtype, workspace,
+                      workspace_bytes, stream, &pa);
+}
+
+int gqa_lse_combine_peer(const float* recv, const unsigned long long* cnt, const unsigned long long* epoch,
+                         int nparts, int64_t slot_floats, int64_t parity_floats, int units, void* o, const int64_t* os,
+                         int batch, int num_heads, int seq_q, int head_dim, int dtype, void* stream) {
+  if (!recv || !cnt || !epoch || nparts < 1 || nparts > kMaxPeers || units < 1) return GQA_ERR_INVALID_ARG;
+  if (batch < 0 || seq_q < 0 || num_heads <= 0 || slot_floats < 0 || parity_floats < nparts * slot_floats)
+    return GQA_ERR_INVALID_ARG;
+  const int64_t rows = (int64_t)batch * num_heads * seq_q;
+  const int64_t acc_off = (2 * rows + 3) / 4 * 4;
+  const int64_t ps[4] = {(int64_t)num_heads * seq_q, (int64_t)seq_q, 1, slot_floats};
+  const int64_t as[5] = {(int64_t)num_heads * seq_q * head_dim, (int64_t)seq_q * head_dim, (int64_t)head_dim,
+                         slot_floats, 1};
+  CombineParams peer{};
+  peer.cnt = cnt;
+  peer.epoch = epoch;
+  peer.units = (unsigned long long)units;
+  peer.parity_stride = parity_floats;
+  return split_reduce_impl(recv, recv + rows, recv + acc_off, o, ps, as, os, batch, num_heads, seq_q, head_dim, nparts,
+                           dtype, stream, &peer);
 }
 
 #ifdef GQA_DEBUG_CHECKS

@@ -69,6 +69,18 @@ struct StreamParams {
   // fp8 K/V (the FP8 instantiation): stored value x scale = real value. k_scale is
   // folded into scale_log2 by the host; v_scale multiplies the accumulators once.
   float v_scale;
+  // Peer exchange (kStreamFusedPartial with npeer > 0, the key-sharded multi-GPU
+  // combine): the unit's combined (m, l, acc) goes to slot my_rank of every rank's
+  // receive buffer -- plain stores, over NVLink for the other ranks -- in the packed
+  // layout [m | l | pad | acc] (l at pk_rows, acc at pk_acc floats), into the parity
+  // (*epoch & 1) half. After the stores, one system-scope release add per rank on
+  // that rank's counter for this source: the ranks' combines wait for it.
+  float* peer_base[kMaxPeers];              // each rank's receive buffer, parity 0 slot 0
+  unsigned long long* peer_cnt[kMaxPeers];  // each rank's counters [world], one per source
+  const unsigned long long* epoch;          // this rank's call counter (gqa_epoch_bump)
+  int64_t peer_slot, peer_parity;           // floats per source slot, per parity half
+  int64_t pk_rows, pk_acc;
+  int npeer, my_rank;
 };
 
 template <int HD>
@@ -883,6 +895,17 @@ __global__ void __launch_bounds__(288, 1)
       uint16_t* dst =
           reinterpret_cast<uint16_t*>(p.o) + b * p.o_sb + (int64_t)head * p.o_sh + (int64_t)pos * p.o_sm + d;
       *reinterpret_cast<uint2*>(dst) = pk;
+    } else if (p.npeer > 0) {
+      const int64_t ro = ((int64_t)b * p.hq + head) * p.seq_q + pos;
+      const int64_t off = (int64_t)(*p.epoch & 1ull) * p.peer_parity + (int64_t)p.my_rank * p.peer_slot;
+      for (int i = 0; i < p.npeer; ++i) {
+        float* dst = p.peer_base[i] + off;
+        *reinterpret_cast<float4*>(dst + p.pk_acc + ro * HD + d) = a;
+        if (d == 0) {
+          dst[ro] = fm[r];
+          dst[p.pk_rows + ro] = fl[r];
+        }
+      }
     } else {
       const int64_t ro = ((int64_t)b * p.hq + head) * p.seq_q + pos;
       *reinterpret_cast<float4*>(p.acc_out + ro * HD + d) = a;
@@ -890,6 +913,16 @@ __global__ void __launch_bounds__(288, 1)
         p.m_out[ro] = fm[r];
         p.l_out[ro] = fl[r];
       }
+    }
+  }
+  if (p.mode == kStreamFusedPartial && p.npeer > 0) {
+    // Every compute thread's peer stores precede thread 0's releases (the barrier
+    // orders them, the release is cumulative): a rank whose counter for this source
+    // has grown sees this unit's rows.
+    GQA_CBAR();
+    if (tid == 0) {
+      for (int i = 0; i < p.npeer; ++i)
+        asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(p.peer_cnt[i] + p.my_rank) : "memory");
     }
   }
   if (tid == 0) p.ws_cnt[unit] = 0u;  // ready for the next call on this workspace

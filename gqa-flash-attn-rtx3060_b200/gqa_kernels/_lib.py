@@ -59,6 +59,18 @@ SIGNATURES = {
     "gqa_paged_kv_append": (_I, [_P, _P, _I64P, _I64P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _F, _P]),
     "gqa_debug_inject": (_I, [_I, _I, ctypes.c_longlong]),
     "gqa_debug_exp2_poly2": (_I, [_P, _P, _I, _P]),
+    "gqa_exchange_alloc": (_I, [_SZ, ctypes.POINTER(_P)]),
+    "gqa_exchange_free": (_I, [_P]),
+    "gqa_ipc_handle": (_I, [_P, _P]),
+    "gqa_ipc_open": (_I, [_P, ctypes.POINTER(_P)]),
+    "gqa_ipc_close": (_I, [_P]),
+    "gqa_epoch_bump": (_I, [_P, _P]),
+    "gqa_partial_units": (_I, [_I, _I, _I, _I, _I, ctypes.POINTER(_I)]),
+    "gqa_partial_peer": (_I, [_P, _P, _P, _I64P, _I64P, _I64P, _I, _I, _I, _I, _I, _I, _I, _I, _F, _I, _I,
+                              ctypes.POINTER(_P), ctypes.POINTER(_P), _I, _I, _P, ctypes.c_int64, ctypes.c_int64,
+                              _P, _SZ, _P]),
+    "gqa_lse_combine_peer": (_I, [_P, _P, _P, _I, ctypes.c_int64, ctypes.c_int64, _I, _P, _I64P, _I, _I, _I, _I, _I,
+                                  _P]),
 }
 
 _lib = None

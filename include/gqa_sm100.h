@@ -164,6 +164,62 @@ int gqa_lse_combine(const float* m_parts, const float* l_parts, const float* acc
                     int num_heads, int seq_q, int head_dim, int dtype, void* stream);
 
 /*
+ * Peer exchange: the key-sharded combine across the GPUs of one node without a
+ * collective library. gqa_partial's outputs go straight from the partial kernel
+ * into every rank's receive buffer (plain stores, over NVLink for the other
+ * ranks), and each rank's combine waits for them in-kernel. It replaces
+ * gqa_partial + an all-gather + gqa_lse_combine with two launches and no
+ * collective call. No reference counterpart (the reference is single-GPU); the
+ * algebra is gqa_kernels/gqa_split.py:137-144's across ranks.
+ *
+ * Each rank holds one exchange buffer (gqa_exchange_alloc, zeroed; it allocates
+ * and synchronises, a setup call): [2 parities][nranks slots][slot_floats
+ * floats] of packed partials [m | l | pad to 16 B | acc] (the layout of
+ * gqa_lse_combine's packed form), then nranks uint64 counters (one per source
+ * rank), then one uint64 call counter (the epoch). Every rank maps the other
+ * ranks' buffers once: gqa_ipc_handle exports this process's buffer as a
+ * GQA_IPC_HANDLE_BYTES handle, gqa_ipc_open maps another process's (CUDA IPC,
+ * same node; never a multicast mapping), gqa_ipc_close unmaps it.
+ *
+ * Per call, on every rank, in this order on one stream:
+ *   gqa_epoch_bump(epoch)       one thread: epoch += 1
+ *   gqa_partial_peer(...)       writes this rank's partial into slot `rank`
+ *                               of parity (epoch & 1) of every rank's buffer,
+ *                               then adds 1 per unit to that rank's counter
+ *                               for this source (system-scope release)
+ *   gqa_lse_combine_peer(...)   waits (bounded) until every source's counter
+ *                               reaches epoch x units, then combines into o
+ * Every rank makes the same calls with the same shapes (so the epochs and unit
+ * counts agree; gqa_partial_units gives the count), and every rank must hold at
+ * least one key (seq_kv_local > 0; else GQA_ERR_UNSUPPORTED: use the all-gather
+ * form, which accepts empty shards). Two parities let a rank start its next
+ * call while another still reads this one: a rank cannot reach the call after
+ * next before every rank has finished this call's combine. A source that never
+ * arrives ends the combine's wait after the wait limit with GQA_ERR_TIMEOUT in
+ * the device error word (gqa_device_error) and o unwritten.
+ * peer_bases[i] / peer_cnts[i] are rank i's buffer and counters as this
+ * process maps them (its own for i == rank); npeer <= 8.
+ */
+#define GQA_IPC_HANDLE_BYTES 64
+int gqa_exchange_alloc(size_t bytes, void** ptr);
+int gqa_exchange_free(void* ptr);
+int gqa_ipc_handle(const void* ptr, void* handle);
+int gqa_ipc_open(const void* handle, void** ptr);
+int gqa_ipc_close(void* ptr);
+int gqa_epoch_bump(unsigned long long* epoch, void* stream);
+int gqa_partial_units(int batch, int num_heads, int num_kv_heads, int seq_q, int head_dim, int* units);
+int gqa_partial_peer(const void* q, const void* k, const void* v, const int64_t* q_strides4, const int64_t* k_strides4,
+                     const int64_t* v_strides4, int batch, int num_heads, int num_kv_heads, int seq_q,
+                     int seq_kv_local, int kv_offset, int seq_kv_total, int head_dim, float scale_log2, int causal,
+                     int dtype, float* const* peer_bases, unsigned long long* const* peer_cnts, int npeer, int rank,
+                     const unsigned long long* epoch, int64_t slot_floats, int64_t parity_floats, void* workspace,
+                     size_t workspace_bytes, void* stream);
+int gqa_lse_combine_peer(const float* recv, const unsigned long long* cnt, const unsigned long long* epoch,
+                         int nparts, int64_t slot_floats, int64_t parity_floats, int units, void* o,
+                         const int64_t* o_strides4, int batch, int num_heads, int seq_q, int head_dim, int dtype,
+                         void* stream);
+
+/*
  * Paged decode: one new query token per sequence attends to that sequence's
  * cached keys, read from a paged K/V cache in the layout vLLM uses,
  * k_cache/v_cache (num_blocks, block_size, num_kv_heads, head_dim), contiguous.

@@ -44,6 +44,29 @@ def _rank_main(rank, world, port, q_ret):
         out = S.seq_sharded_forward(q, k[:, :, k0:k1].contiguous(), v[:, :, k0:k1].contiguous(), k0, Skv)
         res["seq_causal"] = ((out.float() - full.float()).abs().max().item(),
                              (out.float() - full.float()).abs().mean().item())
+        # the same key split with the peer exchange (NVLink stores in the partial
+        # kernel, in-kernel waits in the combine): bit-identical to the all-gather
+        # form over three calls (both parities of the receive buffer, new inputs each)
+        B, Hq, Hkv, Sq, Skv, D = 4, 64, 8, 1, 20000, 128
+        q, k, v = (t.to(dev) for t in make_inputs(B, Hq, Hkv, Sq, Skv, D, seed=8))
+        k0, k1 = S.kv_range(Skv, world, rank)
+        ks, vs = k[:, :, k0:k1].contiguous(), v[:, :, k0:k1].contiguous()
+        ex = S.PeerExchange(q.shape, Hkv, dev)
+        same, worst = True, 0.0
+        try:
+            full = gqa_flash_attn(q, k, v)
+            for call in range(3):
+                qc = q * (1.0 + 0.25 * call)
+                ref = S.seq_sharded_forward(qc, ks, vs, k0, Skv)
+                got = ex.forward(qc, ks, vs, k0, Skv)
+                torch.cuda.synchronize(dev)
+                same = same and torch.equal(got.view(torch.int16), ref.view(torch.int16))
+                if call == 0:
+                    worst = (got.float() - full.float()).abs().max().item()
+        finally:
+            ex.close()
+        res["peer_same"] = same
+        res["peer"] = (worst, 0.0)
         # batch x kv-head units, no communication
         B, Hq, Hkv, Sq, Skv, D = 4, 32, 8, 512, 2048, 128
         q, k, v = (t.to(dev) for t in make_inputs(B, Hq, Hkv, Sq, Skv, D, seed=7))
@@ -75,6 +98,7 @@ def test_sharded_paths_over_nccl():
     for p in procs:
         p.join(timeout=60)
     for rank, res in results.items():
-        for key in ("seq", "seq_causal", "units"):
+        for key in ("seq", "seq_causal", "units", "peer"):
             mx, mn = res[key]
             assert mx < BASELINE_TOL[0] and mn < BASELINE_TOL[1], (rank, key, mx, mn)
+        assert res["peer_same"], rank

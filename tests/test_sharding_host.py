@@ -46,6 +46,29 @@ def test_slice_units_group_heads():
     assert torch.equal(qs, q[1:2, 4:8]) and torch.equal(ks, k[1:2, 1:2])
 
 
+def test_exchange_layout():
+    """The peer exchange buffer: two parities of `world` 16-byte-aligned slots of
+    the packed partial, then the counters and the epoch (8-byte aligned)."""
+    for shape in ((64, 64, 1, 128), (1, 32, 3, 64), (3, 5, 7, 64)):
+        for world in (1, 2, 8):
+            slot, parity, cnt_off, total = S.exchange_layout(shape, world)
+            assert slot == S.packed_size(shape) and slot % 4 == 0
+            assert parity == world * slot and cnt_off == 8 * parity
+            assert cnt_off % 8 == 0 and total == cnt_off + 8 * world + 8
+
+
+def test_peer_exchange_needs_keys_on_every_rank():
+    """kv_range leaves ranks empty past the 64-key blocks; the peer form then does not
+    apply (every rank must take the same form: the all-gather accepts empty shards)."""
+    assert S.all_shards_hold_keys(131072, 8)
+    assert S.all_shards_hold_keys(20000, 8)
+    assert not S.all_shards_hold_keys(64, 2)
+    assert not S.all_shards_hold_keys(300, 8)
+    for skv, world in ((131072, 8), (20000, 8), (64, 2), (300, 8), (512, 8)):
+        expect = all(b > a for a, b in (S.kv_range(skv, world, r) for r in range(world)))
+        assert S.all_shards_hold_keys(skv, world) == expect
+
+
 def test_packed_layout_alignment():
     for shape in [(1, 1, 1, 64), (64, 64, 1, 128), (3, 5, 7, 128)]:
         rows, acc_off, total = S.packed_layout(shape)
