@@ -793,17 +793,13 @@ __global__ void __launch_bounds__(288, 1)
 
   // ---- last CTA of the unit: log-sum-exp combine of all chunk partials.
   // Shared-memory layout (the ring is free now):
-  //   sm_m, sm_l, sm_w [nsplit][rows]  partial m, l and combine weights
-  //   fm, fl [64]                      combined M and L per row
+  //   sm_m, sm_l [nsplit][rows]        partial m and l
   //   cacc [nsplit][rows][HD]          the unit's acc partials, staged by one bulk copy when they fit
   const int64_t ubase = (int64_t)unit * p.nsplit * p.rows;
   const int nsr = p.nsplit * n_rows;
   float* sm_m = reinterpret_cast<float*>(smem);
   float* sm_l = sm_m + nsr;
-  float* sm_w = sm_l + nsr;
-  float* fm = sm_w + nsr;
-  float* fl = fm + 64;
-  const uint32_t small_bytes = ((uint32_t)(3 * nsr + 128) * 4u + 15u) & ~15u;
+  const uint32_t small_bytes = ((uint32_t)(2 * nsr) * 4u + 15u) & ~15u;
   const uint32_t acc_bytes = (uint32_t)nsr * HD * 4u;
   const bool staged = small_bytes + acc_bytes <= (uint32_t)Cfg::kRingBytes;
   float* cacc = reinterpret_cast<float*>(smem + small_bytes);
@@ -821,28 +817,6 @@ __global__ void __launch_bounds__(288, 1)
     sm_l[i] = __ldcg(p.ws_l + ubase + i);
   }
   GQA_CBAR();
-  // Per-row weights over the unit's chunks, w_s = exp2(m_s - max_s m_s): one warp per
-  // row, lanes over chunks, shuffle reductions.
-  for (int r = warp; r < n_rows; r += NW) {
-    float M = -INFINITY;
-    for (int s2 = lane; s2 < p.nsplit; s2 += 32) M = fmaxf(M, sm_m[s2 * n_rows + r]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-    const float Mu = (M == -INFINITY) ? 0.f : M;
-    float L = 0.f;
-    for (int s2 = lane; s2 < p.nsplit; s2 += 32) {
-      const float wt = fast_exp2(sm_m[s2 * n_rows + r] - Mu);
-      sm_w[s2 * n_rows + r] = wt;
-      L += wt * sm_l[s2 * n_rows + r];
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-    if (lane == 0) {
-      fm[r] = M;
-      fl[r] = L;
-    }
-  }
-  GQA_CBAR();
   if (staged) {
     // Waited for even after an abort: the bulk copy must land before the CTA exits.
     volatile int no_abort = 0;
@@ -852,6 +826,13 @@ __global__ void __launch_bounds__(288, 1)
     const int r = idx / per_row, d = (idx - r * per_row) * 4;
     const int g = r / p.block_m, m = r - g * p.block_m, pos = mt * p.block_m + m;
     if (pos >= p.seq_q) continue;
+    // The row's weights over the unit's chunks, w_s = exp2(m_s - max_s m_s), and its
+    // L = sum_s w_s l_s, computed by every thread that writes the row (the same values
+    // in the same order), so no separate weights phase and barrier precede the sum.
+    float M = -INFINITY;
+    for (int s2 = 0; s2 < p.nsplit; ++s2) M = fmaxf(M, sm_m[s2 * n_rows + r]);
+    const float Mu = (M == -INFINITY) ? 0.f : M;
+    float L = 0.f;
     // Splits in batches of kCombBatch: every load of a batch is issued before the
     // first FMA, so a batch costs one load latency instead of one per split. The
     // sum runs in split order, as the reference's reduce does.
@@ -864,13 +845,14 @@ __global__ void __launch_bounds__(288, 1)
 #pragma unroll
         for (int u = 0; u < kCombBatch; ++u) {
           if (s0 + u < p.nsplit) {
-            wt[u] = sm_w[(s0 + u) * n_rows + r];
+            wt[u] = fast_exp2(sm_m[(s0 + u) * n_rows + r] - Mu);
             v[u] = load(s0 + u);
           }
         }
 #pragma unroll
         for (int u = 0; u < kCombBatch; ++u) {
           if (s0 + u < p.nsplit) {
+            L += wt[u] * sm_l[(s0 + u) * n_rows + r];
             a.x += wt[u] * v[u].x;
             a.y += wt[u] * v[u].y;
             a.z += wt[u] * v[u].z;
@@ -888,7 +870,7 @@ __global__ void __launch_bounds__(288, 1)
     }
     const int head = kvh * p.group + g;
     if (p.mode == kStreamFused) {
-      const float inv = 1.f / fl[r];
+      const float inv = 1.f / L;  // L == 0 (no visible key) -> NaN, as the reference
       uint2 pk;
       pk.x = pack2<BF16>(a.x * inv, a.y * inv);
       pk.y = pack2<BF16>(a.z * inv, a.w * inv);
@@ -902,16 +884,16 @@ __global__ void __launch_bounds__(288, 1)
         float* dst = p.peer_base[i] + off;
         *reinterpret_cast<float4*>(dst + p.pk_acc + ro * HD + d) = a;
         if (d == 0) {
-          dst[ro] = fm[r];
-          dst[p.pk_rows + ro] = fl[r];
+          dst[ro] = M;
+          dst[p.pk_rows + ro] = L;
         }
       }
     } else {
       const int64_t ro = ((int64_t)b * p.hq + head) * p.seq_q + pos;
       *reinterpret_cast<float4*>(p.acc_out + ro * HD + d) = a;
       if (d == 0) {
-        p.m_out[ro] = fm[r];
-        p.l_out[ro] = fl[r];
+        p.m_out[ro] = M;
+        p.l_out[ro] = L;
       }
     }
   }
